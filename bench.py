@@ -1,0 +1,389 @@
+#!/usr/bin/env python
+"""Benchmark of the ICTC-O3 hot path on B200: the C128/lmax-3 channelwise tensor product.
+
+Workload: FP32 path-preserving TP, C=128, lmax 3 (23 paths),
+262,144 instances per forward step; forward+VJP (grads of features, harmonics and
+per-instance path weights) at 131,072 instances per step.  Inputs are seeded
+synthetic tensors with the config's distributions: features N(0,1), harmonics of
+uniform random unit vectors, path weights N(0, 1/sqrt(23)), upstream grad N(0,1).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU (torchrun): instances are independent, so every rank runs its own full
+batch with no collective on the data path (weak scaling); the timed region is
+bracketed by barriers and the reported time is the max over ranks.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PACKAGE_ROOT = os.path.join(REPO, "ictc-o3-hp-ascend_b200")
+for _path in (PACKAGE_ROOT, REPO):
+    if _path not in sys.path:
+        sys.path.insert(0, _path)
+
+import torch  # noqa: E402
+
+C, L, PATHS = 128, 3, 23
+FWD_ROWS, VJP_ROWS = 262144, 131072
+FEATURE_W, HARM_W, GATE_W, OUT_W = C * 16, 16, PATHS * C, 12672
+# Algorithmic bytes per instance: each tensor read or written once per pass.
+FWD_BYTES = 4 * (FEATURE_W + HARM_W + GATE_W + OUT_W)                       # 70,720
+BWD_BYTES = 4 * (FEATURE_W + HARM_W + GATE_W + OUT_W) + 4 * (FEATURE_W + HARM_W + GATE_W)
+VJP_BYTES = FWD_BYTES + BWD_BYTES                                           # 161,472
+PUBLISHED_FWD = 2.70e6  # reference, Ascend 910B3, docs/PERFORMANCE.md:19-20
+METRIC = "TP instances/s fwd & fwd+VJP; MACE E+F atom-steps/s at 1/2/4/8 B200"
+WORKLOAD = "ictc_o3 channelwise TP C128/lmax3 FP32 forward, 262,144 instances/step (configs[1])"
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--cpu-seconds", type=float, default=12.0)
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# Distributed plumbing
+# ---------------------------------------------------------------------------
+
+def setup_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(value, world, device):
+    if world == 1:
+        return value
+    t = torch.tensor([value], device=device, dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    QUERY = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, device):
+        self.proc = None
+        try:
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", uuid, f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, AttributeError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        for line in out.strip().splitlines():
+            parts = [v.strip() for v in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, flag in zip(self.NAMES, parts[3:7]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        loaded = [v for v in sm if smax and v > 0.5 * max(smax)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# Inputs
+# ---------------------------------------------------------------------------
+
+def make_inputs(rows, device, seed, requires_grad=False):
+    from ictc_o3.operators import direction_harmonics
+    gen = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(rows, FEATURE_W, device=device, generator=gen)
+    n = torch.nn.functional.normalize(torch.randn(rows, 3, device=device, generator=gen), dim=1)
+    y = torch.cat(direction_harmonics(n, L), -1).contiguous()
+    g = torch.randn(rows, GATE_W, device=device, generator=gen) / PATHS ** 0.5
+    if requires_grad:
+        x.requires_grad_(True), y.requires_grad_(True), g.requires_grad_(True)
+    return x, y, g
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        data = json.load(open(path))
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic(name):
+    """Per-instance DRAM bytes from a committed ncu summary (profiles/<name>), or None."""
+    path = os.path.join(REPO, "profiles", name)
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith("dram_bytes_per_instance:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+def roofline(bytes_per_inst, rows, kernel_ms, traffic_per_inst):
+    peak, kind = peaks()
+    achieved = bytes_per_inst * rows / (kernel_ms * 1e-3) / 1e9
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "peak_kind": kind,
+            "traffic": None if traffic_per_inst is None else round(traffic_per_inst * rows),
+            "algorithmic_bytes": bytes_per_inst * rows}
+
+
+# ---------------------------------------------------------------------------
+# Our arm
+# ---------------------------------------------------------------------------
+
+def time_loop(fn, steps, warmup, world, device):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.current_stream(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    return start.elapsed_time(end)
+
+
+def e2e_forward(op, rows, steps, warmup, device, world):
+    """Public API with host buffers: pinned H2D of inputs, forward, D2H of the output,
+    pipelined in chunks over three streams (copy-in, compute, copy-out)."""
+    chunk = 16384
+    gen = torch.Generator().manual_seed(7)
+    xh = torch.randn(rows, FEATURE_W, generator=gen).pin_memory()
+    nh = torch.nn.functional.normalize(torch.randn(rows, 3, generator=gen), dim=1)
+    from ictc_o3.operators import direction_harmonics
+    yh = torch.cat(direction_harmonics(nh.to(device), L), -1).cpu().pin_memory()
+    gh = (torch.randn(rows, GATE_W, generator=gen) / PATHS ** 0.5).pin_memory()
+    oh = torch.empty(rows, OUT_W).pin_memory()
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    compute = torch.cuda.current_stream(device)
+    nbuf = 3
+    bufs = [(torch.empty(chunk, FEATURE_W, device=device), torch.empty(chunk, HARM_W, device=device),
+             torch.empty(chunk, GATE_W, device=device)) for _ in range(nbuf)]
+    done_compute = [torch.cuda.Event() for _ in range(nbuf)]
+    done_in = [torch.cuda.Event() for _ in range(nbuf)]
+
+    def step():
+        for i, begin in enumerate(range(0, rows, chunk)):
+            b = i % nbuf
+            end = min(begin + chunk, rows)
+            n = end - begin
+            xd, yd, gd = bufs[b]
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(done_compute[b])
+                xd[:n].copy_(xh[begin:end], non_blocking=True)
+                yd[:n].copy_(yh[begin:end], non_blocking=True)
+                gd[:n].copy_(gh[begin:end], non_blocking=True)
+                done_in[b].record(s_in)
+            compute.wait_event(done_in[b])
+            out = op(xd[:n], yd[:n], gd[:n])
+            out.record_stream(s_out)
+            done_compute[b].record(compute)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done_compute[b])
+                oh[begin:end].copy_(out, non_blocking=True)
+        compute.wait_stream(s_out)
+
+    ms = time_loop(step, steps, warmup, world, device) / steps
+    h2d = rows * 4 * (FEATURE_W + HARM_W + GATE_W)
+    d2h = rows * 4 * OUT_W
+    check = float(oh[rows - 1, :8].abs().sum())  # the result is read on the host
+    del check
+    return ms, h2d, d2h
+
+
+def run_ours(args):
+    world, rank, local = setup_dist()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    from ictc_o3.backends.cuda import _native
+    from ictc_o3.operators import EdgeTensorProduct
+    _native.library()
+    op = EdgeTensorProduct.create(channels=C, input_lmax=L, edge_lmax=L, layout="ir_mul", device=device)
+
+    # Forward at 262,144 instances (inputs 7.3 GB, output 13.3 GB: far above L2).
+    x, y, g = make_inputs(FWD_ROWS, device, 1234 + rank)
+    sampler = ClockSampler(device)
+    with torch.no_grad():
+        fwd_ms = time_loop(lambda: op(x, y, g), args.steps, args.warmup, world, device) / args.steps
+    fwd_ms = max_over_ranks(fwd_ms, world, device)
+    del x, y, g
+    torch.cuda.empty_cache()
+
+    # Forward + VJP at 131,072 instances.
+    x, y, g = make_inputs(VJP_ROWS, device, 4321 + rank, requires_grad=True)
+    G = torch.randn(VJP_ROWS, OUT_W, device=device, generator=torch.Generator(device=device).manual_seed(99))
+
+    def fwd_vjp():
+        out = op(x, y, g)
+        torch.autograd.grad(out, [x, y, g], G)
+
+    vjp_ms = time_loop(fwd_vjp, args.steps, args.warmup, world, device) / args.steps
+    vjp_ms = max_over_ranks(vjp_ms, world, device)
+    clocks = sampler.stop()
+    del x, y, g, G
+    torch.cuda.empty_cache()
+
+    e2e_steps = max(2, min(args.steps, 5))
+    e2e_ms, h2d, d2h = e2e_forward(op, FWD_ROWS, e2e_steps, 1, device, world)
+    e2e_ms = max_over_ranks(e2e_ms, world, device)
+
+    if rank != 0:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+    cpu = cpu_baseline(args.cpu_seconds) if world == 1 else None
+    value = world * FWD_ROWS / (fwd_ms * 1e-3)
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "TP instances/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(fwd_ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": round(value / PUBLISHED_FWD, 2),
+        "dtype": "f32", "data": "synthetic (seeded; configs[1] distributions)",
+        "config": {"workload": WORKLOAD, "channels": C, "lmax": L, "paths": PATHS,
+                   "instances_per_step": FWD_ROWS, "per_gpu_instances": FWD_ROWS, "layout": "ir_mul",
+                   "l2": "inputs (7.3 GB) and output (13.3 GB) far exceed the 126 MB L2; no flush needed",
+                   "parallelism": f"replicas x{world} (independent instances, no collective)"},
+        "roofline": roofline(FWD_BYTES, FWD_ROWS, fwd_ms, profiled_traffic("tp_forward_c128_l3.txt")),
+        "fwd_vjp": {"value": round(world * VJP_ROWS / (vjp_ms * 1e-3), 1), "unit": "TP instances/s",
+                    "instances_per_step": VJP_ROWS, "ms_per_step": round(vjp_ms, 4),
+                    "roofline": roofline(VJP_BYTES, VJP_ROWS, vjp_ms, None),
+                    "gpu_launches_per_step": 2},
+        "e2e": {"value": round(world * FWD_ROWS / (e2e_ms * 1e-3), 1), "unit": "TP instances/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "ictc_o3.operators.EdgeTensorProduct.forward, pinned host buffers, chunked H2D/compute/D2H"},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm: the oracle port of the reference CPU module
+# ---------------------------------------------------------------------------
+
+def _cpu_tp_setup(rows, seed):
+    from ictc_o3.basis.ictd_irreps import EdgeWeightedPathPreservingTensorProduct, operator_paths
+    from oracle import tp_oracle
+    owner = EdgeWeightedPathPreservingTensorProduct(C, L, allowed_paths=operator_paths(L, L, L))
+    with torch.no_grad():
+        owner.weight.fill_(1.0)
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn(rows, FEATURE_W, generator=gen)
+    n = torch.nn.functional.normalize(torch.randn(rows, 3, generator=gen), dim=1)
+    y = torch.cat(tp_oracle.direction_harmonics(n, L, tp_oracle.harmonic_tables(L)), -1)
+    g = torch.randn(rows, GATE_W, generator=gen) / PATHS ** 0.5
+    blocks = tp_oracle.split_mul_ir(x, C, L)
+    harm = tp_oracle.split_harm(y, L)
+    return owner, blocks, harm, g.view(rows, PATHS, C), tp_oracle
+
+
+def cpu_baseline(seconds, rows=2048):
+    """Oracle port of the reference CPU TP forward, all host threads, bounded sample."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    owner, blocks, harm, g, tp_oracle = _cpu_tp_setup(rows, 5)
+    with torch.no_grad():
+        tp_oracle.tp_forward(owner, blocks, harm, g)
+        done, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            tp_oracle.tp_forward(owner, blocks, harm, g)
+            done += rows
+        elapsed = time.perf_counter() - t0
+    return {"value": round(done / elapsed, 1), "unit": "TP instances/s", "cores": threads, "kind": "port",
+            "sample": f"{done} instances of C128/lmax3 forward in chunks of {rows} "
+                      f"(oracle/tp_oracle.py, torch CPU FP32, {elapsed:.1f} s)"}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    rows = 2048
+    owner, blocks, harm, g, tp_oracle = _cpu_tp_setup(rows, 17)
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            tp_oracle.tp_forward(owner, blocks, harm, g)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            tp_oracle.tp_forward(owner, blocks, harm, g)
+        elapsed = time.perf_counter() - t0
+    value = args.steps * rows / elapsed
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "TP instances/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * elapsed / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": round(value / PUBLISHED_FWD, 6),
+        "dtype": "f32", "data": "synthetic (seeded; configs[1] distributions)", "impl": "reference",
+        "config": {"workload": WORKLOAD, "channels": C, "lmax": L, "paths": PATHS,
+                   "instances_per_step": rows, "parallelism": "host CPU"},
+        "cpu_baseline": {"value": round(value, 1), "unit": "TP instances/s", "cores": threads, "kind": "port",
+                         "sample": f"each step = {rows} instances of the {FWD_ROWS}-instance workload"},
+        "e2e": {"value": round(value, 1), "unit": "TP instances/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,93 @@
+"""Direction harmonics on the CUDA backend, with analytic first and second adjoints.
+
+Replaces the generated Triton harmonics of the reference
+(``ictc_o3/ops/generated_direction_harmonics.py:43-177``) and evaluates the
+same polynomial map as ``direction_harmonics_all``
+(``ictc_o3/basis/ictd_irreps.py:1113-1168``).
+"""
+import numpy as np
+import torch
+
+from ictc_o3.autograd.adjoint_requirements import required_gradients
+from ictc_o3.basis import ictd_irreps as basis
+from . import _native
+from ._native import ptr, stream_of
+
+_TABLES = {}
+
+
+def harmonic_table(lmax: int, device: torch.device) -> torch.Tensor:
+    """H_l for l = 1..lmax as one flat FP32 device tensor (cached per device)."""
+    key = (int(lmax), str(device))
+    table = _TABLES.get(key)
+    if table is None:
+        flat = np.concatenate([basis.direction_harmonic_table(l).reshape(-1) for l in range(1, lmax + 1)])
+        table = torch.from_numpy(flat.astype(np.float32)).to(device)
+        _TABLES[key] = table
+    return table
+
+
+def _launch(n, lmax, mode, gy=None, hn=None):
+    rows = n.shape[0]
+    width = (lmax + 1) ** 2
+    out0 = torch.empty(rows, 3 if mode == 1 else width, device=n.device, dtype=torch.float32)
+    out1 = torch.empty(rows, 3, device=n.device, dtype=torch.float32) if mode == 2 else None
+    if rows:
+        table = harmonic_table(lmax, n.device)
+        _native.call("ictc_direction_harmonics", ptr(n), ptr(table), ptr(gy), ptr(hn), ptr(out0), ptr(out1),
+                     int(rows), int(lmax), int(mode), stream_of(n))
+    return out0, out1
+
+
+class _Harmonics(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, n, lmax):
+        ctx.lmax = lmax
+        ctx.save_for_backward(n)
+        return _launch(n, lmax, 0)[0]
+
+    @staticmethod
+    def backward(ctx, gy):
+        (n,) = ctx.saved_tensors
+        if not ctx.needs_input_grad[0]:
+            return None, None
+        gy = gy.contiguous()
+        if torch.is_grad_enabled():
+            return _HarmonicsAdjoint.apply(n, gy, ctx.lmax), None
+        return _launch(n, ctx.lmax, 1, gy=gy)[0], None
+
+
+class _HarmonicsAdjoint(torch.autograd.Function):
+    """dn = J(n)^T gY; its backward is the mode-2 kernel (second derivatives)."""
+
+    @staticmethod
+    def forward(ctx, n, gy, lmax):
+        ctx.lmax = lmax
+        ctx.save_for_backward(n, gy)
+        return _launch(n, lmax, 1, gy=gy)[0]
+
+    @staticmethod
+    def backward(ctx, hn):
+        n, gy = ctx.saved_tensors
+        need = required_gradients((n, gy), ctx.needs_input_grad[:2])
+        if not any(need) or hn is None:
+            return None, None, None
+        if torch.is_grad_enabled() and any(t.requires_grad for t in (n, gy, hn)):
+            raise NotImplementedError("third derivatives of the direction harmonics are not provided")
+        d_gy, d_n = _launch(n, ctx.lmax, 2, gy=gy, hn=hn.contiguous())
+        return (d_n if need[0] else None), (d_gy if need[1] else None), None
+
+
+def direction_harmonics(n: torch.Tensor, lmax: int) -> torch.Tensor:
+    """Packed Y(n) [..., (lmax+1)^2] for unit vectors n [..., 3]."""
+    if n.dtype != torch.float32 or n.device.type != "cuda" or n.shape[-1] != 3:
+        raise ValueError("direction harmonics require CUDA FP32 vectors [..., 3]")
+    lead = n.shape[:-1]
+    flat = n.reshape(-1, 3).contiguous()
+    if lmax == 0:
+        return torch.ones(*lead, 1, device=n.device, dtype=n.dtype) + 0 * flat.sum()
+    if torch.is_grad_enabled() and flat.requires_grad:
+        y = _Harmonics.apply(flat, int(lmax))
+    else:
+        y = _launch(flat, int(lmax), 0)[0]
+    return y.reshape(*lead, (lmax + 1) ** 2)

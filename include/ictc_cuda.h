@@ -1,0 +1,120 @@
+/*
+ * ictc_cuda.h -- C ABI of libictc_cuda.so, the B200 (sm_100a) backend for the
+ * ICTC-O3 hot path: the channelwise path-preserving O(3) tensor product (TP),
+ * its adjoints, and the direction harmonics that feed it.
+ *
+ * Conventions
+ *   - Plain C: pointers, sizes, status codes.  No torch or CUDA types; a
+ *     `stream` argument is a cudaStream_t passed as void* (NULL = legacy
+ *     default stream).  Every launch is asynchronous on that stream.
+ *   - All tensors are row-major, contiguous, FP32 device memory.  The caller
+ *     owns every buffer; entry points allocate nothing except inside
+ *     ictc_tp_plan_create (the plan's constant tables).
+ *   - Packed layouts follow the reference's public operator
+ *     (ictc_o3/operators.py:77-127):
+ *       features  [rows, C*(Li+1)^2]  degree-major; inside degree l either
+ *                 ir_mul = [2l+1][C] (layout 0) or mul_ir = [C][2l+1] (layout 1)
+ *       harmonics [rows, (Le+1)^2]    Y_0 | Y_1 | ... (ictc_o3/operators.py:101-105)
+ *       gates     [rows, P*C]         path-major, channel-minor, or NULL
+ *       weight    [P, C]              per-(path, channel) weight, or NULL (= 1)
+ *       out       [rows, C*sum_l count_l*(2l+1)]  ordered by l3, then path
+ *                 offset, then the same inner layout (ictc_o3/operators.py:107-127)
+ *   - Return value: ICTC_OK (0) or a negative ICTC_ERR_*; ictc_last_error()
+ *     returns a message for the calling thread.
+ */
+#ifndef ICTC_CUDA_H
+#define ICTC_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ICTC_ABI_VERSION 1
+
+#define ICTC_OK 0
+#define ICTC_ERR_INVALID (-1)     /* bad pointer, size or shape            */
+#define ICTC_ERR_UNSUPPORTED (-2) /* no kernel for this degree/channel set */
+#define ICTC_ERR_CUDA (-3)        /* CUDA launch or runtime error          */
+#define ICTC_ERR_NOMEM (-4)       /* device or host allocation failed      */
+
+typedef struct ictc_tp_plan ictc_tp_plan;
+
+/* ABI version compiled into the library (ICTC_ABI_VERSION). */
+int ictc_version(void);
+
+/* Message of the last error raised on the calling thread ("" if none). */
+const char* ictc_last_error(void);
+
+/*
+ * Build the constant tables of one path-preserving TP on the current device.
+ * Replaces the reference's cached plan construction
+ * (ictc_o3/backends/ascend/tensor_product.py:9-57, `_plan`), which packs the
+ * owner's CG list (`_get_cg_list`, ictc_o3/basis/ictd_irreps.py:2219-2237)
+ * into sparse routing tables for the native map.
+ *   paths   [num_paths][3] = (l1, l2, l3) in the owner's path order
+ *   cg      concatenation of the normalised per-path CG tensors
+ *           C_p[m1][m2][m3] (float64), cg_len values in total
+ *   cpl_forward / cpl_backward: channels per lane (1, 2 or 4; 0 = default)
+ */
+int ictc_tp_plan_create(int channels, int input_lmax, int edge_lmax, int output_lmax, int layout,
+                        int num_paths, const int32_t* paths, const double* cg, int64_t cg_len,
+                        int cpl_forward, int cpl_backward, ictc_tp_plan** plan);
+
+/* Release a plan (NULL is accepted). */
+int ictc_tp_plan_destroy(ictc_tp_plan* plan);
+
+/* Plan metadata: [num_paths, bond_width, output_width, feature_width,
+ * harmonic_width, cpl_forward, cpl_backward, persistent grid]. */
+int ictc_tp_plan_info(const ictc_tp_plan* plan, int64_t* info, int n);
+
+/*
+ * TP forward, out = TP(features, harmonics, gates * weight).
+ * Replaces mode 0 of the native sparse trilinear map
+ * (ictc_o3/ascendc/op_kernel/weighted_map.cpp:263 `ictc_weighted_map`, bound
+ * at ictc_o3/ascendc/op_host/bindings.cpp:92 `weighted_map`) and the packed
+ * GEMM schedule (ictc_o3/backends/ascend/packed_tensor_product.py:60-80).
+ */
+int ictc_tp_forward(const ictc_tp_plan* plan, const float* features, const float* harmonics,
+                    const float* gates, const float* weight, float* out, int64_t rows, void* stream);
+
+/*
+ * Fused first-order adjoint of ictc_tp_forward for cotangent grad_out.
+ * Any of grad_features / grad_harmonics / grad_gates may be NULL (not
+ * computed); non-NULL outputs are fully overwritten.  With gates == NULL,
+ * grad_gates receives the per-row gradient of the effective weight.
+ * Replaces modes 1-3 (dL, dR, dW) of `ictc_weighted_map`
+ * (ictc_o3/ascendc/op_kernel/weighted_map.cpp:263) and the recursive GEMM
+ * adjoint (ictc_o3/backends/ascend/packed_tensor_product.py:82-110).
+ */
+int ictc_tp_backward(const ictc_tp_plan* plan, const float* features, const float* harmonics,
+                     const float* gates, const float* weight, const float* grad_out,
+                     float* grad_features, float* grad_harmonics, float* grad_gates, int64_t rows,
+                     void* stream);
+
+/* Number of floats in the direction-harmonic table for degrees 1..lmax:
+ * sum_l Dsym(l) * (2l+1), Dsym(l) = (l+1)(l+2)/2. */
+int ictc_harmonics_table_size(int lmax);
+
+/*
+ * ICTC direction harmonics of row vectors n [rows, 3] for l = 0..lmax
+ * (1 <= lmax <= 6), output [rows, (lmax+1)^2] = Y_0 | Y_1 | ... .
+ * table: for l = 1..lmax, H_l[d][m] (row-major, monomials in ICTC order)
+ *        = multinomial_d * (G_l B_l)[d][m] * component_scale_l.
+ * mode 0: out0 = Y(n)                                  (grad_y, grad_dir unused)
+ * mode 1: out0[rows,3] = J(n)^T grad_y                 (first adjoint)
+ * mode 2: out0[rows,W] = J(n) grad_dir,  out1[rows,3] = sum_m grad_y[m] Hess Y_m(n) grad_dir
+ * Replaces the generated Triton harmonics and their analytic adjoints
+ * (ictc_o3/ops/generated_direction_harmonics.py:43-177) and the reference
+ * evaluation direction_harmonics_all (ictc_o3/basis/ictd_irreps.py:1113-1168).
+ */
+int ictc_direction_harmonics(const float* directions, const float* table, const float* grad_y,
+                             const float* grad_dir, float* out0, float* out1, int64_t rows, int lmax,
+                             int mode, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ICTC_CUDA_H */
