@@ -1,0 +1,278 @@
+// C ABI of the tensor-product plans and launches (declared in include/ictc_cuda.h).
+#include "tp_kernels.cuh"
+#include "ictc_cuda.h"
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <vector>
+
+namespace ictc {
+std::vector<Variant> standalone_variants();
+std::vector<Variant> message_variants();
+
+static const std::vector<Variant>& variants() {
+  static const std::vector<Variant> table = [] {
+    std::vector<Variant> all = standalone_variants();
+    std::vector<Variant> msg = message_variants();
+    all.insert(all.end(), msg.begin(), msg.end());
+    return all;
+  }();
+  return table;
+}
+
+static const Variant* find_variant(int li, int le, int lo, int cpl, int layout, int kind) {
+  for (const Variant& v : variants())
+    if (v.li == li && v.le == le && v.lo == lo && v.cpl == cpl && v.layout == layout && v.kind == kind) return &v;
+  return nullptr;
+}
+}  // namespace ictc
+
+using namespace ictc;
+
+struct ictc_tp_plan {
+  int channels, li, le, lo, layout;
+  const Variant* v[kKinds];
+  int cpl[kKinds], slices[kKinds], block[kKinds], grid[kKinds];
+  float* d_coef;
+  int2* d_desc;
+  int device;
+};
+
+static thread_local char g_error[512] = "";
+
+void ictc_set_error(const char* fmt, const char* detail) {
+  snprintf(g_error, sizeof(g_error), fmt, detail ? detail : "");
+}
+
+extern "C" const char* ictc_last_error(void) { return g_error; }
+
+extern "C" int ictc_version(void) { return ICTC_ABI_VERSION; }
+
+// Largest instantiated channels-per-lane <= preferred that divides C, keeps
+// every slice but the last full, and (for grouped kinds) needs <= 8 slices.
+static int pick_cpl(int li, int le, int lo, int layout, int kind, int channels, int preferred) {
+  for (int cpl = preferred; cpl >= 1; cpl /= 2) {
+    if (channels % cpl) continue;
+    if (cpl > 1 && channels < 32 * cpl) continue;
+    int slices = (channels + 32 * cpl - 1) / (32 * cpl);
+    if ((kind == kAdjoint || kind == kMessageAdjoint) && slices > kWarps) continue;
+    if (find_variant(li, le, lo, cpl, layout, kind)) return cpl;
+  }
+  return 0;
+}
+
+extern "C" int ictc_tp_plan_create(int channels, int input_lmax, int edge_lmax, int output_lmax, int layout,
+                                   int num_paths, const int32_t* paths, const double* cg, int64_t cg_len,
+                                   int cpl_forward, int cpl_backward, ictc_tp_plan** out) {
+  if (!out || !paths || !cg) {
+    ictc_set_error("ictc_tp_plan_create: invalid (null) argument%s", "");
+    return ICTC_ERR_INVALID;
+  }
+  *out = nullptr;
+  if (layout != kIrMul && layout != kMulIr) {
+    ictc_set_error("ictc_tp_plan_create: invalid layout, must be 0 (ir_mul) or 1 (mul_ir)%s", "");
+    return ICTC_ERR_INVALID;
+  }
+  if (channels <= 0 || input_lmax < 0 || edge_lmax < 0 || output_lmax < 0 || input_lmax > 6 || edge_lmax > 6 ||
+      output_lmax > 6) {
+    ictc_set_error("ictc_tp_plan_create: invalid channel count or degree%s", "");
+    return ICTC_ERR_INVALID;
+  }
+  const PathTable ref = make_paths(input_lmax, edge_lmax, output_lmax);
+  if (num_paths != ref.np) {
+    ictc_set_error("ictc_tp_plan_create: path list does not match the operator path set%s", "");
+    return ICTC_ERR_UNSUPPORTED;
+  }
+  int64_t expect = 0;
+  for (int p = 0; p < num_paths; ++p) {
+    if (paths[3 * p] != ref.l1[p] || paths[3 * p + 1] != ref.l2[p] || paths[3 * p + 2] != ref.l3[p]) {
+      ictc_set_error("ictc_tp_plan_create: path order differs from the operator path order%s", "");
+      return ICTC_ERR_UNSUPPORTED;
+    }
+    expect += (2 * ref.l1[p] + 1) * (2 * ref.l2[p] + 1) * (2 * ref.l3[p] + 1);
+  }
+  if (cg_len != expect) {
+    ictc_set_error("ictc_tp_plan_create: invalid CG buffer length%s", "");
+    return ICTC_ERR_INVALID;
+  }
+  ictc_tp_plan* plan = new (std::nothrow) ictc_tp_plan();
+  if (!plan) return ICTC_ERR_NOMEM;
+  plan->channels = channels; plan->li = input_lmax; plan->le = edge_lmax; plan->lo = output_lmax;
+  plan->layout = layout;
+  const int rows = ref.out_rows;
+  const int preferred[kKinds] = {cpl_forward > 0 ? cpl_forward : 4, cpl_backward > 0 ? cpl_backward : 2,
+                                 rows * 2 <= 128 ? 2 : 1, cpl_backward > 0 ? cpl_backward : 2};
+  for (int kind = 0; kind < kKinds; ++kind) {
+    int cpl = pick_cpl(input_lmax, edge_lmax, output_lmax, layout, kind, channels, preferred[kind]);
+    plan->v[kind] = cpl ? find_variant(input_lmax, edge_lmax, output_lmax, cpl, layout, kind) : nullptr;
+    if (!plan->v[kind]) {
+      delete plan;
+      ictc_set_error("ictc_tp_plan_create: no kernel for this degree set / channel count%s", "");
+      return ICTC_ERR_UNSUPPORTED;
+    }
+    plan->cpl[kind] = cpl;
+    plan->slices[kind] = (channels + 32 * cpl - 1) / (32 * cpl);
+    plan->block[kind] = (kind == kAdjoint || kind == kMessageAdjoint)
+                            ? 32 * plan->slices[kind] * (kWarps / plan->slices[kind])
+                            : kThreads;
+  }
+  // Re-lay the per-path CG tensors C_p[i][j][k] as [p][i][k][j] and build the
+  // bond column descriptors.
+  std::vector<float> coef(ref.coef_total);
+  std::vector<int2> desc(ref.bond_width);
+  int64_t src = 0;
+  for (int p = 0; p < num_paths; ++p) {
+    int m1 = 2 * ref.l1[p] + 1, m2 = 2 * ref.l2[p] + 1, m3 = 2 * ref.l3[p] + 1;
+    for (int i = 0; i < m1; ++i)
+      for (int j = 0; j < m2; ++j)
+        for (int k = 0; k < m3; ++k)
+          coef[ref.coef_off[p] + (i * m3 + k) * m2 + j] = (float)cg[src + (i * m2 + j) * m3 + k];
+    for (int i = 0; i < m1; ++i)
+      for (int k = 0; k < m3; ++k) {
+        int col = ref.bond_off[p] + i * m3 + k;
+        desc[col].x = (ref.l2[p] * ref.l2[p]) | (m2 << 16);
+        desc[col].y = ref.coef_off[p] + (i * m3 + k) * m2;
+      }
+    src += (int64_t)m1 * m2 * m3;
+  }
+  cudaGetDevice(&plan->device);
+  plan->d_coef = nullptr;
+  plan->d_desc = nullptr;
+  if (cudaMalloc(&plan->d_coef, sizeof(float) * (coef.size() + 4)) != cudaSuccess ||
+      cudaMalloc(&plan->d_desc, sizeof(int2) * (desc.size() + 4)) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(plan->d_coef);
+    delete plan;
+    ictc_set_error("ictc_tp_plan_create: device allocation failed%s", "");
+    return ICTC_ERR_NOMEM;
+  }
+  cudaMemcpy(plan->d_coef, coef.data(), sizeof(float) * coef.size(), cudaMemcpyHostToDevice);
+  cudaMemcpy(plan->d_desc, desc.data(), sizeof(int2) * desc.size(), cudaMemcpyHostToDevice);
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, plan->device);
+  for (int kind = 0; kind < kKinds; ++kind) {
+    const Variant* v = plan->v[kind];
+    int per_sm = 0;
+    cudaFuncSetAttribute(v->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)v->smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v->fn, plan->block[kind], v->smem);
+    plan->grid[kind] = sms * (per_sm < 1 ? 1 : per_sm);
+  }
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) {
+    ictc_set_error("ictc_tp_plan_create: %s", cudaGetErrorString(err));
+    cudaFree(plan->d_coef);
+    cudaFree(plan->d_desc);
+    delete plan;
+    return ICTC_ERR_CUDA;
+  }
+  *out = plan;
+  return ICTC_OK;
+}
+
+extern "C" int ictc_tp_plan_destroy(ictc_tp_plan* plan) {
+  if (!plan) return ICTC_OK;
+  cudaFree(plan->d_coef);
+  cudaFree(plan->d_desc);
+  delete plan;
+  return ICTC_OK;
+}
+
+extern "C" int ictc_tp_plan_info(const ictc_tp_plan* plan, int64_t* info, int n) {
+  if (!plan || !info) {
+    ictc_set_error("ictc_tp_plan_info: invalid (null) argument%s", "");
+    return ICTC_ERR_INVALID;
+  }
+  const Variant* v = plan->v[kForward];
+  int64_t values[12] = {v->np, v->bond_width, v->rows * (int64_t)plan->channels, v->a * (int64_t)plan->channels,
+                        v->b, plan->cpl[kForward], plan->cpl[kAdjoint], plan->grid[kForward],
+                        plan->cpl[kMessageForward], plan->cpl[kMessageAdjoint], plan->grid[kAdjoint],
+                        plan->block[kAdjoint]};
+  for (int t = 0; t < n && t < 12; ++t) info[t] = values[t];
+  return ICTC_OK;
+}
+
+static int launch(const ictc_tp_plan* plan, int kind, TPArgs& args, int64_t units_per_block, void* stream,
+                  const char* what) {
+  args.coef = plan->d_coef;
+  args.desc = plan->d_desc;
+  args.channels = plan->channels;
+  args.slices = plan->slices[kind];
+  if (args.rows <= 0) return ICTC_OK;
+  int64_t work = (args.rows * (kind == kAdjoint || kind == kMessageAdjoint ? 1 : args.slices) + units_per_block - 1) /
+                 units_per_block;
+  int grid = (int)(work < plan->grid[kind] ? work : plan->grid[kind]);
+  const Variant* v = plan->v[kind];
+  v->fn<<<grid, plan->block[kind], v->smem, (cudaStream_t)stream>>>(args);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) {
+    ictc_set_error(what, cudaGetErrorString(err));
+    return ICTC_ERR_CUDA;
+  }
+  return ICTC_OK;
+}
+
+extern "C" int ictc_tp_forward(const ictc_tp_plan* plan, const float* features, const float* harmonics,
+                               const float* gates, const float* weight, float* out, int64_t rows,
+                               void* stream) {
+  if (!plan || rows < 0 || (rows > 0 && (!features || !harmonics || !out))) {
+    ictc_set_error("ictc_tp_forward: invalid argument%s", "");
+    return ICTC_ERR_INVALID;
+  }
+  TPArgs a{};
+  a.features = features; a.harmonics = harmonics; a.gates = gates; a.weight = weight; a.out = out;
+  a.rows = rows;
+  return launch(plan, kForward, a, kWarps, stream, "tensor-product forward launch failed: %s");
+}
+
+extern "C" int ictc_tp_backward(const ictc_tp_plan* plan, const float* features, const float* harmonics,
+                                const float* gates, const float* weight, const float* grad_out,
+                                float* grad_features, float* grad_harmonics, float* grad_gates, int64_t rows,
+                                void* stream) {
+  if (!plan || rows < 0 || (rows > 0 && (!features || !harmonics || !grad_out))) {
+    ictc_set_error("ictc_tp_backward: invalid argument%s", "");
+    return ICTC_ERR_INVALID;
+  }
+  TPArgs a{};
+  a.features = features; a.harmonics = harmonics; a.gates = gates; a.weight = weight; a.grad_out = grad_out;
+  a.grad_features = grad_features; a.grad_harmonics = grad_harmonics; a.grad_gates = grad_gates;
+  a.rows = rows;
+  int groups = plan->block[kAdjoint] / 32 / plan->slices[kAdjoint];
+  return launch(plan, kAdjoint, a, groups, stream, "tensor-product adjoint launch failed: %s");
+}
+
+extern "C" int ictc_tp_message_forward(const ictc_tp_plan* plan, const float* node_features,
+                                       const float* harmonics, const float* gates, const float* weight,
+                                       const float* mask, const int64_t* src, const int64_t* dst_order,
+                                       const int64_t* dst_offsets, float* out, int64_t dst_nodes, void* stream) {
+  if (!plan || dst_nodes < 0 ||
+      (dst_nodes > 0 && (!node_features || !harmonics || !src || !dst_order || !dst_offsets || !out))) {
+    ictc_set_error("ictc_tp_message_forward: invalid argument%s", "");
+    return ICTC_ERR_INVALID;
+  }
+  TPArgs a{};
+  a.features = node_features; a.harmonics = harmonics; a.gates = gates; a.weight = weight; a.mask = mask;
+  a.src = src; a.order = dst_order; a.offsets = dst_offsets; a.out = out; a.rows = dst_nodes;
+  return launch(plan, kMessageForward, a, kWarps, stream, "graph-message forward launch failed: %s");
+}
+
+extern "C" int ictc_tp_message_backward(const ictc_tp_plan* plan, const float* node_features,
+                                        const float* harmonics, const float* gates, const float* weight,
+                                        const float* mask, const int64_t* dst, const int64_t* src_order,
+                                        const int64_t* src_offsets, const float* grad_out,
+                                        float* grad_node_features, float* grad_harmonics, float* grad_gates,
+                                        int64_t src_nodes, void* stream) {
+  if (!plan || src_nodes < 0 ||
+      (src_nodes > 0 && (!node_features || !harmonics || !dst || !src_order || !src_offsets || !grad_out))) {
+    ictc_set_error("ictc_tp_message_backward: invalid argument%s", "");
+    return ICTC_ERR_INVALID;
+  }
+  TPArgs a{};
+  a.features = node_features; a.harmonics = harmonics; a.gates = gates; a.weight = weight; a.mask = mask;
+  a.dst = dst; a.order = src_order; a.offsets = src_offsets; a.grad_out = grad_out;
+  a.grad_features = grad_node_features; a.grad_harmonics = grad_harmonics; a.grad_gates = grad_gates;
+  a.rows = src_nodes;
+  int groups = plan->block[kMessageAdjoint] / 32 / plan->slices[kMessageAdjoint];
+  return launch(plan, kMessageAdjoint, a, groups, stream, "graph-message adjoint launch failed: %s");
+}

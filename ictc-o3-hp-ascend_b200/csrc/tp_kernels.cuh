@@ -1,0 +1,370 @@
+// Kernel templates of the path-preserving ICTC tensor product (standalone and graph message).
+//
+// Math (ictc_o3/basis/ictd_irreps.py:2669-2748, _project_group :2278-2283):
+//   T(x, Y, g)[p, k, c] = g[p,c] w[p,c] sum_{i,j} x_{l1}[i,c] Y_{l2}[j] C_p[i,j,k]
+// factored through bond[p,i,k] = sum_j Y[j] C_p[i,j,k] (the reference backend's
+// bond projection, ictc_o3/backends/ascend/tensor_product.py:35-55).
+// Graph message (ictc_o3/backends/ascend/tensor_product.py:189-218):
+//   out[n] = sum_{e: dst_e = n} mask_e T(x[src_e], Y_e, g_e)
+// evaluated node by node over a destination-sorted CSR, accumulating in
+// registers (no atomics).  Its adjoint walks a source-sorted CSR so the
+// feature gradient of a node is also a register accumulation.
+#pragma once
+
+#include "tp_device.cuh"
+
+namespace ictc {
+
+// ---------------------------------------------------------------------------
+// Standalone forward: one warp per (instance, channel slice); every output
+// block is written straight from registers with streaming stores.
+// ---------------------------------------------------------------------------
+template <int LI, int LE, int LO, int CPL, int LAYOUT>
+__global__ void __launch_bounds__(kThreads) tp_forward_kernel(TPArgs a) {
+  using PS = Paths<LI, LE, LO>;
+  constexpr int A = PS::A, B = PS::B;
+  extern __shared__ __align__(16) float smem[];
+  float* s_coef = smem;
+  int2* s_desc = reinterpret_cast<int2*>(smem + round4(PS::CT));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* s_y = smem + table_floats<PS>() + warp * warp_floats<PS>();
+  float* s_bond = s_y + 32;
+  load_tables<PS>(a, s_coef, s_desc);
+  __syncthreads();
+
+  const int C = a.channels;
+  const int64_t items = a.rows * a.slices;
+  for (int64_t item = (int64_t)blockIdx.x * kWarps + warp; item < items; item += (int64_t)gridDim.x * kWarps) {
+    const int64_t e = item / a.slices;
+    const int s = (int)(item - e * a.slices);
+    const int c0 = (s * 32 + lane) * CPL;
+    const bool active = c0 < C;
+    if (lane < B) s_y[lane] = __ldg(a.harmonics + e * B + lane);
+    float x[A][CPL];
+    load_features<LI, CPL, LAYOUT>(x, a.features + e * A * C, C, c0, active, true);
+    __syncwarp();
+    build_bond<PS>(s_coef, s_desc, s_y, s_bond, lane);
+    __syncwarp();
+    float* orow = a.out + e * (int64_t)PS::ROWS * C;
+    const float* grow = a.gates ? a.gates + e * (int64_t)PS::NP * C : nullptr;
+    static_for<PS::NP>([&](auto pc) {
+      constexpr int p = decltype(pc)::value;
+      constexpr int l1 = PS::T.l1[p], l3 = PS::T.l3[p];
+      constexpr int m1 = 2 * l1 + 1, m3 = 2 * l3 + 1;
+      constexpr int BO = PS::T.bond_off[p], RO = PS::T.out_row[p];
+      float g[CPL];
+#pragma unroll
+      for (int ch = 0; ch < CPL; ++ch) g[ch] = 1.f;
+      if (active) {
+        if (grow) load_vec_stream<CPL>(g, grow + p * C + c0);
+        if (a.weight) {
+          float w[CPL];
+          load_vec<CPL>(w, a.weight + p * C + c0);
+#pragma unroll
+          for (int ch = 0; ch < CPL; ++ch) g[ch] *= w[ch];
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < m3; ++k) {
+        float acc[CPL];
+#pragma unroll
+        for (int ch = 0; ch < CPL; ++ch) acc[ch] = 0.f;
+#pragma unroll
+        for (int i = 0; i < m1; ++i) {
+          const float b = s_bond[BO + i * m3 + k];
+#pragma unroll
+          for (int ch = 0; ch < CPL; ++ch) acc[ch] = fmaf(b, x[l1 * l1 + i][ch], acc[ch]);
+        }
+#pragma unroll
+        for (int ch = 0; ch < CPL; ++ch) acc[ch] *= g[ch];
+        if (active) {
+          if constexpr (LAYOUT == kIrMul) {
+            store_vec_stream<CPL>(orow + (int64_t)(RO + k) * C + c0, acc);
+          } else {
+#pragma unroll
+            for (int ch = 0; ch < CPL; ++ch) __stcs(orow + (int64_t)RO * C + (c0 + ch) * m3 + k, acc[ch]);
+          }
+        }
+      }
+    });
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Graph-message forward over a destination CSR: one warp per (destination
+// node, channel slice); the node's whole output row lives in registers.
+// ---------------------------------------------------------------------------
+template <int LI, int LE, int LO, int CPL, int LAYOUT>
+__global__ void __launch_bounds__(kThreads) tp_message_forward_kernel(TPArgs a) {
+  using PS = Paths<LI, LE, LO>;
+  constexpr int A = PS::A, B = PS::B, ROWS = PS::ROWS;
+  extern __shared__ __align__(16) float smem[];
+  float* s_coef = smem;
+  int2* s_desc = reinterpret_cast<int2*>(smem + round4(PS::CT));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* s_y = smem + table_floats<PS>() + warp * warp_floats<PS>();
+  float* s_bond = s_y + 32;
+  load_tables<PS>(a, s_coef, s_desc);
+  __syncthreads();
+
+  const int C = a.channels;
+  const int64_t items = a.rows * a.slices;
+  for (int64_t item = (int64_t)blockIdx.x * kWarps + warp; item < items; item += (int64_t)gridDim.x * kWarps) {
+    const int64_t n = item / a.slices;
+    const int s = (int)(item - n * a.slices);
+    const int c0 = (s * 32 + lane) * CPL;
+    const bool active = c0 < C;
+    float acc[ROWS][CPL];
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r)
+#pragma unroll
+      for (int ch = 0; ch < CPL; ++ch) acc[r][ch] = 0.f;
+    const int64_t k0 = a.offsets[n], k1 = a.offsets[n + 1];
+    for (int64_t k = k0; k < k1; ++k) {
+      const int64_t e = a.order[k];
+      const int64_t xs = a.src[e];
+      const float m = a.mask ? __ldg(a.mask + e) : 1.f;
+      if (lane < B) s_y[lane] = __ldg(a.harmonics + e * B + lane);
+      float x[A][CPL];
+      load_features<LI, CPL, LAYOUT>(x, a.features + xs * A * C, C, c0, active, false);
+      __syncwarp();
+      build_bond<PS>(s_coef, s_desc, s_y, s_bond, lane);
+      __syncwarp();
+      const float* grow = a.gates ? a.gates + e * (int64_t)PS::NP * C : nullptr;
+      static_for<PS::NP>([&](auto pc) {
+        constexpr int p = decltype(pc)::value;
+        constexpr int l1 = PS::T.l1[p], l3 = PS::T.l3[p];
+        constexpr int m1 = 2 * l1 + 1, m3 = 2 * l3 + 1;
+        constexpr int BO = PS::T.bond_off[p], RO = PS::T.out_row[p];
+        float g[CPL];
+#pragma unroll
+        for (int ch = 0; ch < CPL; ++ch) g[ch] = m;
+        if (active) {
+          if (grow) {
+            float t[CPL];
+            load_vec_stream<CPL>(t, grow + p * C + c0);
+#pragma unroll
+            for (int ch = 0; ch < CPL; ++ch) g[ch] *= t[ch];
+          }
+          if (a.weight) {
+            float w[CPL];
+            load_vec<CPL>(w, a.weight + p * C + c0);
+#pragma unroll
+            for (int ch = 0; ch < CPL; ++ch) g[ch] *= w[ch];
+          }
+        }
+#pragma unroll
+        for (int kk = 0; kk < m3; ++kk) {
+          float base[CPL];
+#pragma unroll
+          for (int ch = 0; ch < CPL; ++ch) base[ch] = 0.f;
+#pragma unroll
+          for (int i = 0; i < m1; ++i) {
+            const float b = s_bond[BO + i * m3 + kk];
+#pragma unroll
+            for (int ch = 0; ch < CPL; ++ch) base[ch] = fmaf(b, x[l1 * l1 + i][ch], base[ch]);
+          }
+#pragma unroll
+          for (int ch = 0; ch < CPL; ++ch) acc[RO + kk][ch] = fmaf(base[ch], g[ch], acc[RO + kk][ch]);
+        }
+      });
+      __syncwarp();
+    }
+    if (active) {
+      float* orow = a.out + n * (int64_t)ROWS * C;
+      if constexpr (LAYOUT == kIrMul) {
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) store_vec<CPL>(orow + (int64_t)r * C + c0, acc[r]);
+      } else {
+        static_for<PS::NP>([&](auto pc) {
+          constexpr int p = decltype(pc)::value;
+          constexpr int m3 = 2 * PS::T.l3[p] + 1;
+          constexpr int RO = PS::T.out_row[p];
+#pragma unroll
+          for (int ch = 0; ch < CPL; ++ch)
+#pragma unroll
+            for (int kk = 0; kk < m3; ++kk) orow[(int64_t)RO * C + (c0 + ch) * m3 + kk] = acc[RO + kk][ch];
+        });
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Fused first-order adjoint, standalone (GRAPH = false: one "node" = one
+// instance) or graph message over a source CSR (GRAPH = true).  For cotangent
+// G of the output,
+//   dx[node, l1, i, c] = sum_{e, p, k} bond_e[p,i,k] h_e[p,k,c]
+//   dY[e, l2, j]       = sum_{p,i,k,c} C_p[i,j,k] x[i,c] h_e[p,k,c]
+//   dgate[e, p, c]     = m_e w[p,c] sum_k G[p,k,c] sum_i bond_e[p,i,k] x[i,c]
+// with h_e = m_e g_e w G[dst_e].  The `slices` warps of a node form a group
+// that walks the same edges; their dY partials meet in shared memory behind a
+// named barrier of the group (deterministic, no global atomics).
+// ---------------------------------------------------------------------------
+template <int LI, int LE, int LO, int CPL, int LAYOUT, bool GRAPH>
+__global__ void __launch_bounds__(kThreads) tp_adjoint_kernel(TPArgs a) {
+  using PS = Paths<LI, LE, LO>;
+  constexpr int A = PS::A, B = PS::B;
+  extern __shared__ __align__(16) float smem[];
+  float* s_coef = smem;
+  int2* s_desc = reinterpret_cast<int2*>(smem + round4(PS::CT));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* s_y = smem + table_floats<PS>() + warp * warp_floats<PS>();
+  float* s_bond = s_y + 32;
+  float* s_dy = smem + table_floats<PS>() + kWarps * warp_floats<PS>();  // [kWarps][B]
+  load_tables<PS>(a, s_coef, s_desc);
+  __syncthreads();
+
+  const int C = a.channels;
+  const int slices = a.slices;
+  const int groups = (int)(blockDim.x >> 5) / slices;
+  const int group = warp / slices, s = warp - group * slices;
+  const int c0 = (s * 32 + lane) * CPL;
+  const bool active = c0 < C;
+  const bool want_dx = a.grad_features != nullptr;
+  const bool want_dy = a.grad_harmonics != nullptr;
+  const bool want_dg = a.grad_gates != nullptr;
+  for (int64_t node = (int64_t)blockIdx.x * groups + group; node < a.rows; node += (int64_t)gridDim.x * groups) {
+    const int64_t k0 = GRAPH ? a.offsets[node] : node;
+    const int64_t k1 = GRAPH ? a.offsets[node + 1] : node + 1;
+    float x[A][CPL];
+    float dx[A][CPL];
+#pragma unroll
+    for (int r = 0; r < A; ++r)
+#pragma unroll
+      for (int ch = 0; ch < CPL; ++ch) dx[r][ch] = 0.f;
+    if constexpr (GRAPH) load_features<LI, CPL, LAYOUT>(x, a.features + node * A * C, C, c0, active, false);
+    for (int64_t k = k0; k < k1; ++k) {
+      const int64_t e = GRAPH ? a.order[k] : k;
+      const int64_t d = GRAPH ? a.dst[e] : k;
+      const float m = (GRAPH && a.mask) ? __ldg(a.mask + e) : 1.f;
+      if constexpr (!GRAPH) load_features<LI, CPL, LAYOUT>(x, a.features + e * A * C, C, c0, active, true);
+      if (lane < B) s_y[lane] = __ldg(a.harmonics + e * B + lane);
+      __syncwarp();
+      build_bond<PS>(s_coef, s_desc, s_y, s_bond, lane);
+      __syncwarp();
+      float dyp[B];
+#pragma unroll
+      for (int j = 0; j < B; ++j) dyp[j] = 0.f;
+      const float* Grow = a.grad_out + d * (int64_t)PS::ROWS * C;
+      const float* grow = a.gates ? a.gates + e * (int64_t)PS::NP * C : nullptr;
+      float* dgrow = want_dg ? a.grad_gates + e * (int64_t)PS::NP * C : nullptr;
+      static_for<PS::NP>([&](auto pc) {
+        constexpr int p = decltype(pc)::value;
+        constexpr int l1 = PS::T.l1[p], l2 = PS::T.l2[p], l3 = PS::T.l3[p];
+        constexpr int m1 = 2 * l1 + 1, m2 = 2 * l2 + 1, m3 = 2 * l3 + 1;
+        constexpr int BO = PS::T.bond_off[p], RO = PS::T.out_row[p], CO = PS::T.coef_off[p];
+        float G[m3][CPL];
+        float gate[CPL], w[CPL];
+#pragma unroll
+        for (int ch = 0; ch < CPL; ++ch) { gate[ch] = 1.f; w[ch] = 1.f; }
+        if (active) {
+          load_out_block<CPL, LAYOUT, RO, m3>(G, Grow, C, c0, !GRAPH);
+          if (grow) load_vec_stream<CPL>(gate, grow + p * C + c0);
+          if (a.weight) load_vec<CPL>(w, a.weight + p * C + c0);
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < m3; ++kk)
+#pragma unroll
+            for (int ch = 0; ch < CPL; ++ch) G[kk][ch] = 0.f;
+        }
+        if (want_dg) {
+          float dg[CPL];
+#pragma unroll
+          for (int ch = 0; ch < CPL; ++ch) dg[ch] = 0.f;
+#pragma unroll
+          for (int kk = 0; kk < m3; ++kk) {
+#pragma unroll
+            for (int ch = 0; ch < CPL; ++ch) {
+              float base = 0.f;
+#pragma unroll
+              for (int i = 0; i < m1; ++i) base = fmaf(s_bond[BO + i * m3 + kk], x[l1 * l1 + i][ch], base);
+              dg[ch] = fmaf(G[kk][ch], base, dg[ch]);
+            }
+          }
+          // d(effective gate) * d(effective gate)/d(gate): m w with gates, m without.
+#pragma unroll
+          for (int ch = 0; ch < CPL; ++ch) dg[ch] *= grow ? m * w[ch] : m;
+          if (active) store_vec<CPL>(dgrow + p * C + c0, dg);
+        }
+        float h[m3][CPL];
+#pragma unroll
+        for (int kk = 0; kk < m3; ++kk)
+#pragma unroll
+          for (int ch = 0; ch < CPL; ++ch) h[kk][ch] = G[kk][ch] * (gate[ch] * w[ch] * m);
+        if (want_dx) {
+#pragma unroll
+          for (int i = 0; i < m1; ++i)
+#pragma unroll
+            for (int kk = 0; kk < m3; ++kk) {
+              const float b = s_bond[BO + i * m3 + kk];
+#pragma unroll
+              for (int ch = 0; ch < CPL; ++ch) dx[l1 * l1 + i][ch] = fmaf(b, h[kk][ch], dx[l1 * l1 + i][ch]);
+            }
+        }
+        if (want_dy) {
+#pragma unroll
+          for (int i = 0; i < m1; ++i)
+#pragma unroll
+            for (int kk = 0; kk < m3; ++kk) {
+              float t = 0.f;
+#pragma unroll
+              for (int ch = 0; ch < CPL; ++ch) t = fmaf(x[l1 * l1 + i][ch], h[kk][ch], t);
+#pragma unroll
+              for (int j = 0; j < m2; ++j)
+                dyp[l2 * l2 + j] = fmaf(s_coef[CO + (i * m3 + kk) * m2 + j], t, dyp[l2 * l2 + j]);
+            }
+        }
+      });
+      if (want_dy) {
+        float mine = 0.f;
+#pragma unroll
+        for (int j = 0; j < B; ++j) {
+          const float v = warp_sum(dyp[j]);
+          if (lane == j) mine = v;
+        }
+        if (slices == 1) {
+          if (lane < B) a.grad_harmonics[e * B + lane] = mine;
+        } else {
+          if (lane < B) s_dy[warp * B + lane] = mine;
+          group_barrier(1 + group, 32 * slices);
+          if (s == 0 && lane < B) {
+            float total = 0.f;
+            for (int t = 0; t < slices; ++t) total += s_dy[(warp + t) * B + lane];
+            a.grad_harmonics[e * B + lane] = total;
+          }
+          group_barrier(1 + group, 32 * slices);
+        }
+      }
+      __syncwarp();
+    }
+    if (want_dx && active) store_features<LI, CPL, LAYOUT>(a.grad_features + node * A * C, dx, C, c0);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Variant registry (host side)
+// ---------------------------------------------------------------------------
+using KernelFn = void (*)(TPArgs);
+
+enum Kind : int { kForward = 0, kAdjoint = 1, kMessageForward = 2, kMessageAdjoint = 3, kKinds = 4 };
+
+struct Variant {
+  int li, le, lo, cpl, layout, kind;
+  KernelFn fn;
+  int np, bond_width, coef_total, rows, a, b;
+  size_t smem;
+};
+
+template <int LI, int LE, int LO, int CPL, int LAYOUT>
+Variant make_variant(int kind, KernelFn fn) {
+  using PS = Paths<LI, LE, LO>;
+  Variant v;
+  v.li = LI; v.le = LE; v.lo = LO; v.cpl = CPL; v.layout = LAYOUT; v.kind = kind; v.fn = fn;
+  v.np = PS::NP; v.bond_width = PS::BW; v.coef_total = PS::CT; v.rows = PS::ROWS; v.a = PS::A; v.b = PS::B;
+  v.smem = sizeof(float) * smem_floats<PS>();
+  return v;
+}
+
+}  // namespace ictc

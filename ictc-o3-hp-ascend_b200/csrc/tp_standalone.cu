@@ -1,0 +1,34 @@
+// Instantiations of the standalone tensor-product kernels (forward, fused adjoint).
+#include "tp_kernels.cuh"
+
+#include <vector>
+
+namespace ictc {
+
+template <int LI, int LE, int LO, int LAYOUT>
+static void add_standalone(std::vector<Variant>& out) {
+  out.push_back(make_variant<LI, LE, LO, 1, LAYOUT>(kForward, tp_forward_kernel<LI, LE, LO, 1, LAYOUT>));
+  out.push_back(make_variant<LI, LE, LO, 2, LAYOUT>(kForward, tp_forward_kernel<LI, LE, LO, 2, LAYOUT>));
+  out.push_back(make_variant<LI, LE, LO, 4, LAYOUT>(kForward, tp_forward_kernel<LI, LE, LO, 4, LAYOUT>));
+  out.push_back(make_variant<LI, LE, LO, 1, LAYOUT>(kAdjoint, tp_adjoint_kernel<LI, LE, LO, 1, LAYOUT, false>));
+  out.push_back(make_variant<LI, LE, LO, 2, LAYOUT>(kAdjoint, tp_adjoint_kernel<LI, LE, LO, 2, LAYOUT, false>));
+}
+
+template <int LI, int LE, int LO>
+static void add_both(std::vector<Variant>& out) {
+  add_standalone<LI, LE, LO, kIrMul>(out);
+  add_standalone<LI, LE, LO, kMulIr>(out);
+}
+
+std::vector<Variant> standalone_variants() {
+  std::vector<Variant> out;
+  add_both<0, 1, 1>(out);
+  add_both<1, 1, 1>(out);
+  add_both<0, 2, 2>(out);
+  add_both<2, 2, 2>(out);
+  add_both<0, 3, 3>(out);
+  add_both<3, 3, 3>(out);
+  return out;
+}
+
+}  // namespace ictc

@@ -27,6 +27,8 @@ _SIGNATURES = {
     "ictc_tp_plan_info": [_p, ctypes.POINTER(_i64), _i],
     "ictc_tp_forward": [_p, _p, _p, _p, _p, _p, _i64, _p],
     "ictc_tp_backward": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p],
+    "ictc_tp_message_forward": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p],
+    "ictc_tp_message_backward": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p],
     "ictc_harmonics_table_size": [_i],
     "ictc_direction_harmonics": [_p, _p, _p, _p, _p, _p, _i64, _i, _i, _p],
 }

@@ -58,6 +58,9 @@ class TPPlan:
         _native.call("ictc_tp_plan_info", handle, info, 8)
         (self.np_, self.bond_width, self.output_width, self.feature_width, self.harmonic_width,
          self.cpl_forward, self.cpl_backward, self.grid) = (int(v) for v in info)
+        extra = (ctypes.c_int64 * 12)()
+        _native.call("ictc_tp_plan_info", handle, extra, 12)
+        self.cpl_message_forward, self.cpl_message_backward = int(extra[8]), int(extra[9])
 
     def __del__(self):
         handle = getattr(self, "handle", None)
@@ -98,27 +101,40 @@ def _check(*tensors):
             raise ValueError("CUDA tensor-product operands must be contiguous FP32 CUDA tensors")
 
 
+class StandaloneOp:
+    """Row-wise TP: out[e] = T(x[e], y[e], g[e])."""
+
+    def __init__(self, plan: TPPlan):
+        self.plan = plan
+
+    def forward(self, x, y, g, w):
+        plan, rows = self.plan, x.shape[0]
+        out = torch.empty(rows, plan.output_width, device=x.device, dtype=torch.float32)
+        if rows:
+            _check(x, y, g, w)
+            _native.call("ictc_tp_forward", plan.handle, ptr(x), ptr(y), ptr(g), ptr(w), ptr(out),
+                         int(rows), stream_of(x))
+        return out
+
+    def adjoint(self, x, y, g, w, grad, need):
+        plan, rows = self.plan, x.shape[0]
+        dx = torch.empty_like(x) if need[0] else None
+        dy = torch.empty_like(y) if need[1] else None
+        dg = (torch.empty(rows, plan.num_paths * plan.channels, device=x.device, dtype=torch.float32)
+              if need[2] else None)
+        if rows and any(need):
+            _check(x, y, g, w, grad)
+            _native.call("ictc_tp_backward", plan.handle, ptr(x), ptr(y), ptr(g), ptr(w), ptr(grad),
+                         ptr(dx), ptr(dy), ptr(dg), int(rows), stream_of(x))
+        return dx, dy, dg
+
+
 def raw_forward(plan: TPPlan, x, y, g, w):
-    rows = x.shape[0]
-    out = torch.empty(rows, plan.output_width, device=x.device, dtype=torch.float32)
-    if rows:
-        _check(x, y, g, w)
-        _native.call("ictc_tp_forward", plan.handle, ptr(x), ptr(y), ptr(g), ptr(w), ptr(out),
-                     int(rows), stream_of(x))
-    return out
+    return StandaloneOp(plan).forward(x, y, g, w)
 
 
 def raw_backward(plan: TPPlan, x, y, g, w, grad, need):
-    rows = x.shape[0]
-    dx = torch.empty_like(x) if need[0] else None
-    dy = torch.empty_like(y) if need[1] else None
-    dg = (torch.empty(rows, plan.num_paths * plan.channels, device=x.device, dtype=torch.float32)
-          if need[2] else None)
-    if rows and any(need):
-        _check(x, y, g, w, grad)
-        _native.call("ictc_tp_backward", plan.handle, ptr(x), ptr(y), ptr(g), ptr(w), ptr(grad),
-                     ptr(dx), ptr(dy), ptr(dg), int(rows), stream_of(x))
-    return dx, dy, dg
+    return StandaloneOp(plan).adjoint(x, y, g, w, grad, need)
 
 
 def _add(a, b):
@@ -130,17 +146,18 @@ def _add(a, b):
 
 
 # ---------------------------------------------------------------------------
-# Autograd
+# Autograd (shared by the standalone TP and the graph message: both are
+# trilinear in (x, y, g) with every other input fixed)
 # ---------------------------------------------------------------------------
 
 class _Product(torch.autograd.Function):
     """out = T(x, y, g); ``w`` is a constant per-(path, channel) factor of g."""
 
     @staticmethod
-    def forward(ctx, plan, w, x, y, g):
-        ctx.plan, ctx.w, ctx.has_g = plan, w, g is not None
+    def forward(ctx, op, w, x, y, g):
+        ctx.op, ctx.w, ctx.has_g = op, w, g is not None
         ctx.save_for_backward(x, y, g)
-        return raw_forward(plan, x, y, g, w)
+        return op.forward(x, y, g, w)
 
     @staticmethod
     def backward(ctx, grad):
@@ -150,38 +167,38 @@ class _Product(torch.autograd.Function):
             return None, None, None, None, None
         grad = grad.contiguous()
         if torch.is_grad_enabled():
-            dx, dy, dg = _Adjoint.apply(ctx.plan, ctx.w, x, y, g, grad, need)
+            dx, dy, dg = _Adjoint.apply(ctx.op, ctx.w, x, y, g, grad, need)
         else:
-            dx, dy, dg = raw_backward(ctx.plan, x, y, g, ctx.w, grad, need)
+            dx, dy, dg = ctx.op.adjoint(x, y, g, ctx.w, grad, need)
         return None, None, dx, dy, (dg if ctx.has_g else None)
 
 
-def product(plan, w, x, y, g):
+def product(op, w, x, y, g):
     if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in (x, y, g)):
-        return _Product.apply(plan, w, x, y, g)
-    return raw_forward(plan, x, y, g, w)
+        return _Product.apply(op, w, x, y, g)
+    return op.forward(x, y, g, w)
 
 
-def adjoint(plan, w, x, y, g, grad, need):
+def adjoint(op, w, x, y, g, grad, need):
     if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in (x, y, g, grad)):
-        return _Adjoint.apply(plan, w, x, y, g, grad, tuple(need))
-    return raw_backward(plan, x, y, g, w, grad, need)
+        return _Adjoint.apply(op, w, x, y, g, grad, tuple(need))
+    return op.adjoint(x, y, g, w, grad, need)
 
 
 class _Adjoint(torch.autograd.Function):
     """(A_x, A_y, A_g) = first adjoints of T at cotangent G; differentiable again."""
 
     @staticmethod
-    def forward(ctx, plan, w, x, y, g, grad, need):
+    def forward(ctx, op, w, x, y, g, grad, need):
         ctx.set_materialize_grads(False)
-        ctx.plan, ctx.w, ctx.need = plan, w, tuple(need)
+        ctx.op, ctx.w = op, w
         ctx.save_for_backward(x, y, g, grad)
-        return raw_backward(plan, x, y, g, w, grad, need)
+        return op.adjoint(x, y, g, w, grad, need)
 
     @staticmethod
     def backward(ctx, hx, hy, hg):
         x, y, g, grad = ctx.saved_tensors
-        plan, w = ctx.plan, ctx.w
+        op, w = ctx.op, ctx.w
         need = required_gradients((x, y, g, grad), ctx.needs_input_grad[2:6])
         hx = None if hx is None else hx.contiguous()
         hy = None if hy is None else hy.contiguous()
@@ -190,26 +207,26 @@ class _Adjoint(torch.autograd.Function):
         # hx: <hx, A_x(y, g, G)> = <G, T(hx, y, g)>
         if hx is not None:
             if need[1] or (need[2] and g is not None):
-                _, ay, ag = adjoint(plan, w, hx, y, g, grad, (False, need[1], need[2] and g is not None))
+                _, ay, ag = adjoint(op, w, hx, y, g, grad, (False, need[1], need[2] and g is not None))
                 gy, gg = _add(gy, ay), _add(gg, ag)
             if need[3]:
-                gG = _add(gG, product(plan, w, hx, y, g))
+                gG = _add(gG, product(op, w, hx, y, g))
         # hy: <hy, A_y(x, g, G)> = <G, T(x, hy, g)>
         if hy is not None:
             if need[0] or (need[2] and g is not None):
-                ax, _, ag = adjoint(plan, w, x, hy, g, grad, (need[0], False, need[2] and g is not None))
+                ax, _, ag = adjoint(op, w, x, hy, g, grad, (need[0], False, need[2] and g is not None))
                 gx, gg = _add(gx, ax), _add(gg, ag)
             if need[3]:
-                gG = _add(gG, product(plan, w, x, hy, g))
+                gG = _add(gG, product(op, w, x, hy, g))
         # hg: <hg, A_g(x, y, G)> = <G, T(x, y, hg)>; without gates the third
         # output is the derivative of the effective weight itself.
         if hg is not None:
             wh = w if g is not None else None
             if need[0] or need[1]:
-                ax, ay, _ = adjoint(plan, wh, x, y, hg, grad, (need[0], need[1], False))
+                ax, ay, _ = adjoint(op, wh, x, y, hg, grad, (need[0], need[1], False))
                 gx, gy = _add(gx, ax), _add(gy, ay)
             if need[3]:
-                gG = _add(gG, product(plan, wh, x, y, hg))
+                gG = _add(gG, product(op, wh, x, y, hg))
         return (None, None, gx if need[0] else None, gy if need[1] else None,
                 gg if need[2] else None, gG if need[3] else None, None)
 
@@ -239,7 +256,7 @@ def packed_product(owner, layout, features, harmonics, gates):
     w, g = _weight_and_gates(owner, gates, rows)
     if features.shape[1] != plan.feature_width or harmonics.shape != (rows, plan.harmonic_width):
         raise ValueError("Packed features/harmonics do not match the tensor-product degrees")
-    return product(plan, w, features.contiguous(), harmonics.contiguous(), g)
+    return product(StandaloneOp(plan), w, features.contiguous(), harmonics.contiguous(), g)
 
 
 def tensor_product(owner, features: Dict[int, torch.Tensor], harmonics: Dict[int, torch.Tensor],

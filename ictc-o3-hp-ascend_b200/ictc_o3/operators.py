@@ -119,6 +119,45 @@ class EdgeTensorProduct(torch.nn.Module):
         return packed_product(self.tp, self.layout, features, harmonics, gates)
 
 
+class PackedGraphMessage(EdgeTensorProduct):
+    """Packed node gather, CUDA TP and destination aggregation (reference ``operators.py:141-163``)."""
+
+    def __init__(self, *args, edge_chunk_size=16384, **kwargs):
+        super().__init__(*args, **kwargs)
+        _positive_integer(edge_chunk_size, "edge_chunk_size")
+        self.edge_chunk_size = edge_chunk_size
+
+    @classmethod
+    def create(cls, *, edge_chunk_size=16384, **kwargs):
+        op = EdgeTensorProduct.create(**kwargs)
+        return cls(op.tp, input_lmax=op.input_lmax, edge_lmax=op.edge_lmax,
+                   layout=op.layout, edge_chunk_size=edge_chunk_size)
+
+    def forward(self, features, harmonics, gates, src, dst, mask=None):
+        for value in (src, dst):
+            if value.ndim != 1 or value.dtype != torch.int64 or value.device != features.device:
+                raise ValueError("Graph indices must be int64 vectors on the CUDA device")
+        if dst.shape != src.shape:
+            raise ValueError("Source and destination index shapes must match")
+        require_cuda_fp32(features, self.tp.weight)
+        if features.ndim != 2 or features.shape[1] != self.tp.channels * (self.input_lmax + 1) ** 2:
+            raise ValueError("Packed features must have shape [E,C*(L_in+1)^2]")
+        if harmonics.shape != (src.numel(), (self.edge_lmax + 1) ** 2):
+            raise ValueError("Harmonics must have shape [E,(L_edge+1)^2]")
+        require_cuda_fp32(harmonics, gates)
+        from ictc_o3.backends.cuda.message import packed_graph_message
+        return packed_graph_message(self.tp, self.layout, features, harmonics, gates, src, dst, mask)
+
+
+class GraphMessage(PackedGraphMessage):
+    """Dictionary block interface for the same graph message map."""
+
+    def forward(self, features, harmonics, gates, src, dst, mask=None):
+        from ictc_o3.backends.cuda.message import graph_message
+        return graph_message(self.tp, features, harmonics, gates, src, dst, mask,
+                             edge_chunk_size=self.edge_chunk_size)
+
+
 def direction_harmonics(directions, lmax, *, policy="auto"):
     """Y_l(n) for l <= lmax as a list of [..., 2l+1] (reference ``operators.py:173-186``).
 
@@ -140,4 +179,5 @@ def normalized_silu(features, scale=1.):
     return F.silu(features) * float(scale)
 
 
-__all__ = ["EdgeTensorProduct", "direction_harmonics", "normalized_silu", "strict_fp32"]
+__all__ = ["EdgeTensorProduct", "PackedGraphMessage", "GraphMessage", "direction_harmonics",
+           "normalized_silu", "strict_fp32"]

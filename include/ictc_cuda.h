@@ -65,8 +65,9 @@ int ictc_tp_plan_create(int channels, int input_lmax, int edge_lmax, int output_
 /* Release a plan (NULL is accepted). */
 int ictc_tp_plan_destroy(ictc_tp_plan* plan);
 
-/* Plan metadata: [num_paths, bond_width, output_width, feature_width,
- * harmonic_width, cpl_forward, cpl_backward, persistent grid]. */
+/* Plan metadata (first n of): [num_paths, bond_width, output_width,
+ * feature_width, harmonic_width, cpl_forward, cpl_backward, forward grid,
+ * cpl_message_forward, cpl_message_backward, adjoint grid, adjoint block]. */
 int ictc_tp_plan_info(const ictc_tp_plan* plan, int64_t* info, int n);
 
 /*
@@ -92,6 +93,39 @@ int ictc_tp_backward(const ictc_tp_plan* plan, const float* features, const floa
                      const float* gates, const float* weight, const float* grad_out,
                      float* grad_features, float* grad_harmonics, float* grad_gates, int64_t rows,
                      void* stream);
+
+/*
+ * Graph message, out[n] = sum_{e: dst_e = n} mask_e * TP(node_features[src_e],
+ * harmonics_e, gates_e * weight) for n < dst_nodes, evaluated over a
+ * destination-sorted CSR (dst_order: edge ids grouped by destination,
+ * dst_offsets [dst_nodes+1]).  Every output row is written (zero for nodes
+ * without edges); no atomics.  mask [E] may be NULL.  Indices must be valid
+ * (src_e < rows of node_features, dst_e < dst_nodes); the host validates them.
+ * Replaces the fused gather / TP / FP32-atomic scatter of `ictc_weighted_map`
+ * in graph mode (ictc_o3/ascendc/op_kernel/weighted_map.cpp:178-233), the
+ * gate-and-scatter epilogue (ictc_o3/ascendc/op_kernel/epilogue.cpp:192) and
+ * the chunked message schedules (ictc_o3/ascendc/graph.py:22-76,
+ * ictc_o3/backends/ascend/channel_message.py:35-216).
+ */
+int ictc_tp_message_forward(const ictc_tp_plan* plan, const float* node_features, const float* harmonics,
+                            const float* gates, const float* weight, const float* mask, const int64_t* src,
+                            const int64_t* dst_order, const int64_t* dst_offsets, float* out, int64_t dst_nodes,
+                            void* stream);
+
+/*
+ * Fused first-order adjoint of ictc_tp_message_forward for cotangent grad_out
+ * [dst_nodes, output_width], walked over a source-sorted CSR (src_order,
+ * src_offsets [src_nodes+1]).  Writes grad_node_features [src_nodes, ...]
+ * (zero rows for nodes without edges), grad_harmonics [E, B] and grad_gates
+ * [E, P*C] (any may be NULL).  Replaces the epilogue adjoints
+ * (ictc_o3/ascendc/op_kernel/epilogue.cpp:192 modes 1-2) and the capacity
+ * first-order backward (ictc_o3/backends/ascend/capacity_adjoint.py:56-148).
+ */
+int ictc_tp_message_backward(const ictc_tp_plan* plan, const float* node_features, const float* harmonics,
+                             const float* gates, const float* weight, const float* mask, const int64_t* dst,
+                             const int64_t* src_order, const int64_t* src_offsets, const float* grad_out,
+                             float* grad_node_features, float* grad_harmonics, float* grad_gates,
+                             int64_t src_nodes, void* stream);
 
 /* Number of floats in the direction-harmonic table for degrees 1..lmax:
  * sum_l Dsym(l) * (2l+1), Dsym(l) = (l+1)(l+2)/2. */
