@@ -128,6 +128,8 @@ def packed_graph_message(owner, layout, features, harmonics, gates, src, dst, ma
     src_nodes = features.shape[0]
     dst_nodes = destination_nodes(owner, src_nodes) if dst_nodes is None else int(dst_nodes)
     edges = src.numel()
+    if owner.weight.device != features.device:
+        raise ValueError("The tensor-product weight must be on the operands' CUDA device")
     plan = get_plan(owner, layout, features.device)
     if features.shape[1] != plan.feature_width or harmonics.shape != (edges, plan.harmonic_width):
         raise ValueError("Packed features/harmonics do not match the message degrees")

@@ -238,6 +238,8 @@ class _Adjoint(torch.autograd.Function):
 def _weight_and_gates(owner, gates, rows):
     """Split owner.weight * gates into (kernel weight, differentiable gates)."""
     weight = owner.weight
+    if gates is not None and weight.device != gates.device:
+        raise ValueError("The tensor-product weight must be on the operands' CUDA device")
     channels, paths = int(owner.channels), int(owner.num_paths)
     if gates is not None:
         gates = gates.reshape(rows, paths * channels)
@@ -252,6 +254,8 @@ def _weight_and_gates(owner, gates, rows):
 def packed_product(owner, layout, features, harmonics, gates):
     """Packed public layout: features [E, C(Li+1)^2] -> [E, output_width]."""
     rows = features.shape[0]
+    if owner.weight.device != features.device:
+        raise ValueError("The tensor-product weight must be on the operands' CUDA device")
     plan = get_plan(owner, layout, features.device)
     w, g = _weight_and_gates(owner, gates, rows)
     if features.shape[1] != plan.feature_width or harmonics.shape != (rows, plan.harmonic_width):

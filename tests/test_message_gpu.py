@@ -55,6 +55,8 @@ def test_message_random_against_oracle(shape, graph, cuda_device):
     gen = torch.Generator().manual_seed(nodes * 131 + edges + C)
     owner = make_owner(C, li, le, lo)
     owner._cuda_destination_nodes = dst_nodes
+    owner_dev = make_owner(C, li, le, lo).to(cuda_device)
+    owner_dev._cuda_destination_nodes = dst_nodes
     P = owner.num_paths
     src, dst = _random_graph(gen, nodes, edges, dst_nodes)
     x = torch.randn(nodes, C * (li + 1) ** 2, generator=gen)
@@ -92,7 +94,7 @@ def test_message_random_against_oracle(shape, graph, cuda_device):
         yc = y.to(dev).requires_grad_(True)
         gc = gates.to(dev).requires_grad_(True)
         Gc = Gi.to(dev).contiguous().requires_grad_(True)
-        out = packed_graph_message(owner, layout, xc, yc, gc, src.to(dev), dst.to(dev), mask.to(dev))
+        out = packed_graph_message(owner_dev, layout, xc, yc, gc, src.to(dev), dst.to(dev), mask.to(dev))
         assert out.shape == (dst_nodes, owner.output_width)
         got = out if layout == "mul_ir" else ir_mul_to_mul_ir(out, C, output_degrees(owner))
         assert_close(got.detach().cpu(), ref.detach(), FWD_TOL, 1e-3, f"{shape} {graph} {layout} fwd")
@@ -140,6 +142,7 @@ def test_message_config3_scale_sampled(cuda_device):
     from ictc_o3.backends.cuda.message import packed_graph_message
     C, L, nodes, deg = 64, 2, 16384, 52
     owner = make_owner(C, L, L, L)
+    owner_dev = make_owner(C, L, L, L).to(cuda_device)
     dev = cuda_device
     gen = torch.Generator(device=dev).manual_seed(5)
     edges = nodes * deg
@@ -152,7 +155,7 @@ def test_message_config3_scale_sampled(cuda_device):
     from ictc_o3.backends.cuda.geometry import direction_harmonics
     y = direction_harmonics(n, L).requires_grad_(True)
     gates = (torch.randn(edges, owner.num_paths * C, device=dev, generator=gen) / 11 ** 0.5).requires_grad_(True)
-    out = packed_graph_message(owner, "ir_mul", x, y, gates, src, dst)
+    out = packed_graph_message(owner_dev, "ir_mul", x, y, gates, src, dst)
     G = torch.randn_like(out)
     dx, dy, dg = torch.autograd.grad(out, [x, y, gates], G)
     rows = torch.randint(0, nodes, (32,), device=dev, generator=gen)
