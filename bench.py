@@ -48,6 +48,9 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
+    p.add_argument("--profile", action="store_true",
+                   help="kernel timing only (forward, then forward+VJP) for ncu captures: no e2e, no CPU baseline")
+    p.add_argument("--rows", type=int, default=0, help="instances per step in --profile mode (0 = config sizes)")
     return p.parse_args()
 
 
@@ -377,9 +380,36 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_profile(args):
+    """Forward then forward+VJP at one size, printing per-step times (for ncu command lines)."""
+    device = torch.device("cuda", 0)
+    from ictc_o3.backends.cuda import _native
+    from ictc_o3.operators import EdgeTensorProduct
+    _native.library()
+    op = EdgeTensorProduct.create(channels=C, input_lmax=L, edge_lmax=L, layout="ir_mul", device=device)
+    rows_f = args.rows or FWD_ROWS
+    rows_v = args.rows or VJP_ROWS
+    x, y, g = make_inputs(rows_f, device, 1)
+    with torch.no_grad():
+        fwd_ms = time_loop(lambda: op(x, y, g), args.steps, args.warmup, 1, device) / args.steps
+    del x, y, g
+    x, y, g = make_inputs(rows_v, device, 2, requires_grad=True)
+    G = torch.randn(rows_v, OUT_W, device=device)
+
+    def fwd_vjp():
+        torch.autograd.grad(op(x, y, g), [x, y, g], G)
+
+    vjp_ms = time_loop(fwd_vjp, args.steps, args.warmup, 1, device) / args.steps
+    print(json.dumps({"profile": True, "fwd_rows": rows_f, "fwd_ms": round(fwd_ms, 4),
+                      "fwd_GBps": round(FWD_BYTES * rows_f / fwd_ms / 1e6, 1), "vjp_rows": rows_v,
+                      "vjp_ms": round(vjp_ms, 4), "vjp_GBps": round(VJP_BYTES * rows_v / vjp_ms / 1e6, 1)}))
+
+
 def main():
     args = parse_args()
-    if args.impl == "reference":
+    if args.profile:
+        run_profile(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -3,6 +3,7 @@
 #include "ictc_cuda.h"
 
 #include <cstdio>
+#include <cmath>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -35,6 +36,7 @@ struct ictc_tp_plan {
   int channels, li, le, lo, layout;
   const Variant* v[kKinds];
   int cpl[kKinds], slices[kKinds], block[kKinds], grid[kKinds];
+  std::vector<float> coef;  // host copy of the dense CG table (kernel-parameter source)
   float* d_coef;
   int2* d_desc;
   int device;
@@ -118,6 +120,26 @@ extern "C" int ictc_tp_plan_create(int channels, int input_lmax, int edge_lmax, 
                             ? 32 * plan->slices[kind] * (kWarps / plan->slices[kind])
                             : kThreads;
   }
+  // The kernels skip structurally zero CG terms of the frozen ICTC basis at
+  // compile time; reject a CG table with a significant entry outside that pattern.
+  {
+    int64_t off = 0;
+    for (int p = 0; p < num_paths; ++p) {
+      int l1 = ref.l1[p], l2 = ref.l2[p], l3 = ref.l3[p];
+      int m1 = 2 * l1 + 1, m2 = 2 * l2 + 1, m3 = 2 * l3 + 1;
+      double peak = 0.0;
+      for (int t = 0; t < m1 * m2 * m3; ++t) peak = fmax(peak, fabs(cg[off + t]));
+      for (int i = 0; i < m1; ++i)
+        for (int j = 0; j < m2; ++j)
+          for (int k = 0; k < m3; ++k)
+            if (!cg_nonzero(l1, l2, l3, i, j, k) && fabs(cg[off + (i * m2 + j) * m3 + k]) > 1e-10 * peak) {
+              delete plan;
+              ictc_set_error("ictc_tp_plan_create: CG tensors are not in the frozen ICTC basis pattern%s", "");
+              return ICTC_ERR_UNSUPPORTED;
+            }
+      off += (int64_t)m1 * m2 * m3;
+    }
+  }
   // Re-lay the per-path CG tensors C_p[i][j][k] as [p][i][k][j] and build the
   // bond column descriptors.
   std::vector<float> coef(ref.coef_total);
@@ -137,6 +159,7 @@ extern "C" int ictc_tp_plan_create(int channels, int input_lmax, int edge_lmax, 
       }
     src += (int64_t)m1 * m2 * m3;
   }
+  plan->coef = coef;
   cudaGetDevice(&plan->device);
   plan->d_coef = nullptr;
   plan->d_desc = nullptr;
@@ -204,8 +227,7 @@ static int launch(const ictc_tp_plan* plan, int kind, TPArgs& args, int64_t unit
                  units_per_block;
   int grid = (int)(work < plan->grid[kind] ? work : plan->grid[kind]);
   const Variant* v = plan->v[kind];
-  v->fn<<<grid, plan->block[kind], v->smem, (cudaStream_t)stream>>>(args);
-  cudaError_t err = cudaGetLastError();
+  cudaError_t err = v->launch(args, plan->coef.data(), grid, plan->block[kind], v->smem, (cudaStream_t)stream);
   if (err != cudaSuccess) {
     ictc_set_error(what, cudaGetErrorString(err));
     return ICTC_ERR_CUDA;

@@ -36,6 +36,16 @@ struct TPArgs {
   int slices;                           // ceil(C / (32 * CPL))
 };
 
+// Kernel parameters of the adjoint kernels: the launch arguments plus the dense
+// CG table [p][i][k][j].  Passed by value (__grid_constant__), the coefficients
+// sit in the constant parameter bank, so compile-time-indexed reads become
+// FFMA constant operands instead of shared-memory loads.
+template <int CT>
+struct CoefParams {
+  TPArgs a;
+  float coef[CT];
+};
+
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 
@@ -75,6 +85,48 @@ __device__ __forceinline__ void build_bond(const float* s_coef, const int2* s_de
   }
 }
 
+// Rows of one input degree l: x[i][ch] = feature (l, i, c0 + ch) of a packed row.
+template <int l, int CPL, int LAYOUT>
+__device__ __forceinline__ void load_degree(float (&x)[2 * l + 1][CPL], const float* row, int channels, int c0,
+                                            bool active, bool stream) {
+  constexpr int m = 2 * l + 1;
+  if (!active) {
+#pragma unroll
+    for (int i = 0; i < m; ++i)
+#pragma unroll
+      for (int ch = 0; ch < CPL; ++ch) x[i][ch] = 0.f;
+    return;
+  }
+  if constexpr (LAYOUT == kIrMul) {
+#pragma unroll
+    for (int i = 0; i < m; ++i) {
+      const float* src = row + (int64_t)(l * l + i) * channels + c0;
+      if (stream) load_vec_stream<CPL>(x[i], src);
+      else load_vec<CPL>(x[i], src);
+    }
+  } else {
+    const float* blk = row + l * l * channels;
+#pragma unroll
+    for (int ch = 0; ch < CPL; ++ch)
+#pragma unroll
+      for (int i = 0; i < m; ++i) x[i][ch] = __ldg(blk + (c0 + ch) * m + i);
+  }
+}
+
+template <int l, int CPL, int LAYOUT>
+__device__ __forceinline__ void store_degree(float* row, const float (&x)[2 * l + 1][CPL], int channels, int c0) {
+  constexpr int m = 2 * l + 1;
+  if constexpr (LAYOUT == kIrMul) {
+#pragma unroll
+    for (int i = 0; i < m; ++i) store_vec<CPL>(row + (int64_t)(l * l + i) * channels + c0, x[i]);
+  } else {
+#pragma unroll
+    for (int ch = 0; ch < CPL; ++ch)
+#pragma unroll
+      for (int i = 0; i < m; ++i) row[l * l * channels + (c0 + ch) * m + i] = x[i][ch];
+  }
+}
+
 template <int LI, int CPL, int LAYOUT>
 __device__ __forceinline__ void load_features(float (&x)[(LI + 1) * (LI + 1)][CPL], const float* row,
                                               int channels, int c0, bool active, bool stream) {
@@ -86,41 +138,34 @@ __device__ __forceinline__ void load_features(float (&x)[(LI + 1) * (LI + 1)][CP
     return;
   }
   if constexpr (LAYOUT == kIrMul) {
-    if (stream) {
 #pragma unroll
-      for (int r = 0; r < (LI + 1) * (LI + 1); ++r) load_vec_stream<CPL>(x[r], row + (int64_t)r * channels + c0);
-    } else {
-#pragma unroll
-      for (int r = 0; r < (LI + 1) * (LI + 1); ++r) load_vec<CPL>(x[r], row + (int64_t)r * channels + c0);
+    for (int r = 0; r < (LI + 1) * (LI + 1); ++r) {
+      if (stream) load_vec_stream<CPL>(x[r], row + (int64_t)r * channels + c0);
+      else load_vec<CPL>(x[r], row + (int64_t)r * channels + c0);
     }
   } else {
-    static_for<LI + 1>([&](auto lc) {
-      constexpr int l = decltype(lc)::value;
-      constexpr int m = 2 * l + 1;
-      const float* blk = row + l * l * channels;
+#pragma unroll
+    for (int l = 0; l <= LI; ++l)
 #pragma unroll
       for (int ch = 0; ch < CPL; ++ch)
 #pragma unroll
-        for (int i = 0; i < m; ++i) x[l * l + i][ch] = __ldg(blk + (c0 + ch) * m + i);
-    });
+        for (int i = 0; i < 2 * l + 1; ++i) x[l * l + i][ch] = __ldg(row + l * l * channels + (c0 + ch) * (2 * l + 1) + i);
   }
 }
 
 template <int LI, int CPL, int LAYOUT>
-__device__ __forceinline__ void store_features(float* row, const float (&x)[(LI + 1) * (LI + 1)][CPL],
-                                               int channels, int c0) {
+__device__ __forceinline__ void store_features(float* row, const float (&x)[(LI + 1) * (LI + 1)][CPL], int channels,
+                                               int c0) {
   if constexpr (LAYOUT == kIrMul) {
 #pragma unroll
     for (int r = 0; r < (LI + 1) * (LI + 1); ++r) store_vec<CPL>(row + (int64_t)r * channels + c0, x[r]);
   } else {
-    static_for<LI + 1>([&](auto lc) {
-      constexpr int l = decltype(lc)::value;
-      constexpr int m = 2 * l + 1;
+#pragma unroll
+    for (int l = 0; l <= LI; ++l)
 #pragma unroll
       for (int ch = 0; ch < CPL; ++ch)
 #pragma unroll
-        for (int i = 0; i < m; ++i) row[l * l * channels + (c0 + ch) * m + i] = x[l * l + i][ch];
-    });
+        for (int i = 0; i < 2 * l + 1; ++i) row[l * l * channels + (c0 + ch) * (2 * l + 1) + i] = x[l * l + i][ch];
   }
 }
 

@@ -11,6 +11,7 @@
 // feature gradient of a node is also a register accumulation.
 #pragma once
 
+#include "cg_pattern.h"
 #include "tp_device.cuh"
 
 namespace ictc {
@@ -40,52 +41,59 @@ __global__ void __launch_bounds__(kThreads) tp_forward_kernel(TPArgs a) {
     const int c0 = (s * 32 + lane) * CPL;
     const bool active = c0 < C;
     if (lane < B) s_y[lane] = __ldg(a.harmonics + e * B + lane);
-    float x[A][CPL];
-    load_features<LI, CPL, LAYOUT>(x, a.features + e * A * C, C, c0, active, true);
     __syncwarp();
     build_bond<PS>(s_coef, s_desc, s_y, s_bond, lane);
     __syncwarp();
+    const float* xrow = a.features + e * A * C;
     float* orow = a.out + e * (int64_t)PS::ROWS * C;
     const float* grow = a.gates ? a.gates + e * (int64_t)PS::NP * C : nullptr;
-    static_for<PS::NP>([&](auto pc) {
-      constexpr int p = decltype(pc)::value;
-      constexpr int l1 = PS::T.l1[p], l3 = PS::T.l3[p];
-      constexpr int m1 = 2 * l1 + 1, m3 = 2 * l3 + 1;
-      constexpr int BO = PS::T.bond_off[p], RO = PS::T.out_row[p];
-      float g[CPL];
+    // Paths are ordered by input degree, so only one degree's rows are live at a time.
+    static_for<LI + 1>([&](auto lc) {
+      constexpr int l1 = decltype(lc)::value;
+      constexpr int m1 = 2 * l1 + 1;
+      float x[m1][CPL];
+      load_degree<l1, CPL, LAYOUT>(x, xrow, C, c0, active, true);
+      static_for<PS::NP>([&](auto pc) {
+        constexpr int p = decltype(pc)::value;
+        if constexpr (PS::T.l1[p] == decltype(lc)::value) {
+          constexpr int m3 = 2 * PS::T.l3[p] + 1;
+          constexpr int BO = PS::T.bond_off[p], RO = PS::T.out_row[p];
+          float g[CPL];
 #pragma unroll
-      for (int ch = 0; ch < CPL; ++ch) g[ch] = 1.f;
-      if (active) {
-        if (grow) load_vec_stream<CPL>(g, grow + p * C + c0);
-        if (a.weight) {
-          float w[CPL];
-          load_vec<CPL>(w, a.weight + p * C + c0);
+          for (int ch = 0; ch < CPL; ++ch) g[ch] = 1.f;
+          if (active) {
+            if (grow) load_vec_stream<CPL>(g, grow + p * C + c0);
+            if (a.weight) {
+              float w[CPL];
+              load_vec<CPL>(w, a.weight + p * C + c0);
 #pragma unroll
-          for (int ch = 0; ch < CPL; ++ch) g[ch] *= w[ch];
-        }
-      }
+              for (int ch = 0; ch < CPL; ++ch) g[ch] *= w[ch];
+            }
+          }
 #pragma unroll
-      for (int k = 0; k < m3; ++k) {
-        float acc[CPL];
+          for (int k = 0; k < m3; ++k) {
+            float acc[CPL];
 #pragma unroll
-        for (int ch = 0; ch < CPL; ++ch) acc[ch] = 0.f;
+            for (int ch = 0; ch < CPL; ++ch) acc[ch] = 0.f;
 #pragma unroll
-        for (int i = 0; i < m1; ++i) {
-          const float b = s_bond[BO + i * m3 + k];
+            for (int i = 0; i < m1; ++i) {
+              const float b = s_bond[BO + i * m3 + k];
 #pragma unroll
-          for (int ch = 0; ch < CPL; ++ch) acc[ch] = fmaf(b, x[l1 * l1 + i][ch], acc[ch]);
-        }
+              for (int ch = 0; ch < CPL; ++ch) acc[ch] = fmaf(b, x[i][ch], acc[ch]);
+            }
 #pragma unroll
-        for (int ch = 0; ch < CPL; ++ch) acc[ch] *= g[ch];
-        if (active) {
-          if constexpr (LAYOUT == kIrMul) {
-            store_vec_stream<CPL>(orow + (int64_t)(RO + k) * C + c0, acc);
-          } else {
+            for (int ch = 0; ch < CPL; ++ch) acc[ch] *= g[ch];
+            if (active) {
+              if constexpr (LAYOUT == kIrMul) {
+                store_vec_stream<CPL>(orow + (int64_t)(RO + k) * C + c0, acc);
+              } else {
 #pragma unroll
-            for (int ch = 0; ch < CPL; ++ch) __stcs(orow + (int64_t)RO * C + (c0 + ch) * m3 + k, acc[ch]);
+                for (int ch = 0; ch < CPL; ++ch) __stcs(orow + (int64_t)RO * C + (c0 + ch) * m3 + k, acc[ch]);
+              }
+            }
           }
         }
-      }
+      });
     });
     __syncwarp();
   }
@@ -203,9 +211,10 @@ __global__ void __launch_bounds__(kThreads) tp_message_forward_kernel(TPArgs a) 
 // named barrier of the group (deterministic, no global atomics).
 // ---------------------------------------------------------------------------
 template <int LI, int LE, int LO, int CPL, int LAYOUT, bool GRAPH>
-__global__ void __launch_bounds__(kThreads) tp_adjoint_kernel(TPArgs a) {
+__global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoint_kernel(const __grid_constant__ CoefParams<Paths<LI, LE, LO>::CT> P) {
   using PS = Paths<LI, LE, LO>;
   constexpr int A = PS::A, B = PS::B;
+  const TPArgs& a = P.a;
   extern __shared__ __align__(16) float smem[];
   float* s_coef = smem;
   int2* s_desc = reinterpret_cast<int2*>(smem + round4(PS::CT));
@@ -225,21 +234,110 @@ __global__ void __launch_bounds__(kThreads) tp_adjoint_kernel(TPArgs a) {
   const bool want_dx = a.grad_features != nullptr;
   const bool want_dy = a.grad_harmonics != nullptr;
   const bool want_dg = a.grad_gates != nullptr;
+
+  // Adjoint of one path for one edge.  Rows XO + i of xl / dxl hold the path's
+  // input degree and its gradient accumulators (XO = l1^2 for whole-row arrays,
+  // 0 for one-degree arrays); dyp: this lane's partial dY of the edge.
+  auto path_adjoint = [&](auto pc, auto xo, auto& xl, auto& dxl, auto& dyp, const float* Grow,
+                          const float* grow, float* dgrow, float m) {
+    constexpr int p = decltype(pc)::value;
+    constexpr int XO = decltype(xo)::value;
+    constexpr int l1 = PS::T.l1[p], l2 = PS::T.l2[p], l3 = PS::T.l3[p];
+    constexpr int m1 = 2 * l1 + 1, m2 = 2 * l2 + 1, m3 = 2 * l3 + 1;
+    constexpr int BO = PS::T.bond_off[p], RO = PS::T.out_row[p], CO = PS::T.coef_off[p];
+    float G[m3][CPL];
+    float gate[CPL], w[CPL];
+#pragma unroll
+    for (int ch = 0; ch < CPL; ++ch) { gate[ch] = 1.f; w[ch] = 1.f; }
+    if (active) {
+      load_out_block<CPL, LAYOUT, RO, m3>(G, Grow, C, c0, !GRAPH);
+      if (grow) load_vec_stream<CPL>(gate, grow + p * C + c0);
+      if (a.weight) load_vec<CPL>(w, a.weight + p * C + c0);
+    } else {
+#pragma unroll
+      for (int kk = 0; kk < m3; ++kk)
+#pragma unroll
+        for (int ch = 0; ch < CPL; ++ch) G[kk][ch] = 0.f;
+    }
+    float h[m3][CPL], base[m3][CPL];
+#pragma unroll
+    for (int kk = 0; kk < m3; ++kk)
+#pragma unroll
+      for (int ch = 0; ch < CPL; ++ch) {
+        h[kk][ch] = G[kk][ch] * (gate[ch] * w[ch] * m);
+        base[kk][ch] = 0.f;
+      }
+    // One read of each bond value serves both the gate adjoint (base) and dx.
+#pragma unroll
+    for (int i = 0; i < m1; ++i)
+#pragma unroll
+      for (int kk = 0; kk < m3; ++kk) {
+        const float b = s_bond[BO + i * m3 + kk];
+#pragma unroll
+        for (int ch = 0; ch < CPL; ++ch) {
+          base[kk][ch] = fmaf(b, xl[XO + i][ch], base[kk][ch]);
+          dxl[XO + i][ch] = fmaf(b, h[kk][ch], dxl[XO + i][ch]);
+        }
+      }
+    if (want_dg) {
+      float dg[CPL];
+#pragma unroll
+      for (int ch = 0; ch < CPL; ++ch) {
+        float v = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < m3; ++kk) v = fmaf(G[kk][ch], base[kk][ch], v);
+        // d(effective gate) * d(effective gate)/d(gate): m w with gates, m without.
+        dg[ch] = v * (grow ? m * w[ch] : m);
+      }
+      if (active) store_vec<CPL>(dgrow + p * C + c0, dg);
+    }
+    if (want_dy) {
+      // dY_{l2}[j] += sum_{i,k} C_p[i,j,k] sum_c x[i,c] h[k,c]; structurally zero CG
+      // terms are skipped at compile time, the values come from the parameter bank.
+      static_for<m1>([&](auto ic) {
+        constexpr int i = decltype(ic)::value;
+        static_for<m3>([&](auto kc) {
+          constexpr int kk = decltype(kc)::value;
+          float t = 0.f;
+#pragma unroll
+          for (int ch = 0; ch < CPL; ++ch) t = fmaf(xl[XO + i][ch], h[kk][ch], t);
+          static_for<m2>([&](auto jc) {
+            constexpr int j = decltype(jc)::value;
+            if constexpr (CgNonzero<l1, l2, l3, i, j, kk>::value)
+              dyp[l2 * l2 + j] = fmaf(P.coef[CO + (i * m3 + kk) * m2 + j], t, dyp[l2 * l2 + j]);
+          });
+        });
+      });
+    }
+  };
+
+  // dY of one edge: warp all-reduce, then a shared-memory sum over the group's slices.
+  auto finish_dy = [&](auto& dyp, int64_t e) {
+    float mine = 0.f;
+#pragma unroll
+    for (int j = 0; j < B; ++j) {
+      const float v = warp_sum(dyp[j]);
+      if (lane == j) mine = v;
+    }
+    if (slices == 1) {
+      if (lane < B) a.grad_harmonics[e * B + lane] = mine;
+    } else {
+      if (lane < B) s_dy[warp * B + lane] = mine;
+      group_barrier(1 + group, 32 * slices);
+      if (s == 0 && lane < B) {
+        float total = 0.f;
+        for (int t = 0; t < slices; ++t) total += s_dy[(warp + t) * B + lane];
+        a.grad_harmonics[e * B + lane] = total;
+      }
+      group_barrier(1 + group, 32 * slices);
+    }
+  };
+
   for (int64_t node = (int64_t)blockIdx.x * groups + group; node < a.rows; node += (int64_t)gridDim.x * groups) {
-    const int64_t k0 = GRAPH ? a.offsets[node] : node;
-    const int64_t k1 = GRAPH ? a.offsets[node + 1] : node + 1;
-    float x[A][CPL];
-    float dx[A][CPL];
-#pragma unroll
-    for (int r = 0; r < A; ++r)
-#pragma unroll
-      for (int ch = 0; ch < CPL; ++ch) dx[r][ch] = 0.f;
-    if constexpr (GRAPH) load_features<LI, CPL, LAYOUT>(x, a.features + node * A * C, C, c0, active, false);
-    for (int64_t k = k0; k < k1; ++k) {
-      const int64_t e = GRAPH ? a.order[k] : k;
-      const int64_t d = GRAPH ? a.dst[e] : k;
-      const float m = (GRAPH && a.mask) ? __ldg(a.mask + e) : 1.f;
-      if constexpr (!GRAPH) load_features<LI, CPL, LAYOUT>(x, a.features + e * A * C, C, c0, active, true);
+    if constexpr (!GRAPH) {
+      // Standalone: one instance; paths are ordered by input degree, so one
+      // degree's rows and gradients are live at a time.
+      const int64_t e = node;
       if (lane < B) s_y[lane] = __ldg(a.harmonics + e * B + lane);
       __syncwarp();
       build_bond<PS>(s_coef, s_desc, s_y, s_bond, lane);
@@ -247,123 +345,121 @@ __global__ void __launch_bounds__(kThreads) tp_adjoint_kernel(TPArgs a) {
       float dyp[B];
 #pragma unroll
       for (int j = 0; j < B; ++j) dyp[j] = 0.f;
-      const float* Grow = a.grad_out + d * (int64_t)PS::ROWS * C;
+      const float* Grow = a.grad_out + e * (int64_t)PS::ROWS * C;
       const float* grow = a.gates ? a.gates + e * (int64_t)PS::NP * C : nullptr;
       float* dgrow = want_dg ? a.grad_gates + e * (int64_t)PS::NP * C : nullptr;
-      static_for<PS::NP>([&](auto pc) {
-        constexpr int p = decltype(pc)::value;
-        constexpr int l1 = PS::T.l1[p], l2 = PS::T.l2[p], l3 = PS::T.l3[p];
-        constexpr int m1 = 2 * l1 + 1, m2 = 2 * l2 + 1, m3 = 2 * l3 + 1;
-        constexpr int BO = PS::T.bond_off[p], RO = PS::T.out_row[p], CO = PS::T.coef_off[p];
-        float G[m3][CPL];
-        float gate[CPL], w[CPL];
+      static_for<LI + 1>([&](auto lc) {
+        constexpr int l1 = decltype(lc)::value;
+        constexpr int m1 = 2 * l1 + 1;
+        float xl[m1][CPL], dxl[m1][CPL];
+        load_degree<l1, CPL, LAYOUT>(xl, a.features + e * A * C, C, c0, active, true);
 #pragma unroll
-        for (int ch = 0; ch < CPL; ++ch) { gate[ch] = 1.f; w[ch] = 1.f; }
-        if (active) {
-          load_out_block<CPL, LAYOUT, RO, m3>(G, Grow, C, c0, !GRAPH);
-          if (grow) load_vec_stream<CPL>(gate, grow + p * C + c0);
-          if (a.weight) load_vec<CPL>(w, a.weight + p * C + c0);
-        } else {
+        for (int i = 0; i < m1; ++i)
 #pragma unroll
-          for (int kk = 0; kk < m3; ++kk)
-#pragma unroll
-            for (int ch = 0; ch < CPL; ++ch) G[kk][ch] = 0.f;
-        }
-        if (want_dg) {
-          float dg[CPL];
-#pragma unroll
-          for (int ch = 0; ch < CPL; ++ch) dg[ch] = 0.f;
-#pragma unroll
-          for (int kk = 0; kk < m3; ++kk) {
-#pragma unroll
-            for (int ch = 0; ch < CPL; ++ch) {
-              float base = 0.f;
-#pragma unroll
-              for (int i = 0; i < m1; ++i) base = fmaf(s_bond[BO + i * m3 + kk], x[l1 * l1 + i][ch], base);
-              dg[ch] = fmaf(G[kk][ch], base, dg[ch]);
-            }
-          }
-          // d(effective gate) * d(effective gate)/d(gate): m w with gates, m without.
-#pragma unroll
-          for (int ch = 0; ch < CPL; ++ch) dg[ch] *= grow ? m * w[ch] : m;
-          if (active) store_vec<CPL>(dgrow + p * C + c0, dg);
-        }
-        float h[m3][CPL];
-#pragma unroll
-        for (int kk = 0; kk < m3; ++kk)
-#pragma unroll
-          for (int ch = 0; ch < CPL; ++ch) h[kk][ch] = G[kk][ch] * (gate[ch] * w[ch] * m);
-        if (want_dx) {
-#pragma unroll
-          for (int i = 0; i < m1; ++i)
-#pragma unroll
-            for (int kk = 0; kk < m3; ++kk) {
-              const float b = s_bond[BO + i * m3 + kk];
-#pragma unroll
-              for (int ch = 0; ch < CPL; ++ch) dx[l1 * l1 + i][ch] = fmaf(b, h[kk][ch], dx[l1 * l1 + i][ch]);
-            }
-        }
-        if (want_dy) {
-#pragma unroll
-          for (int i = 0; i < m1; ++i)
-#pragma unroll
-            for (int kk = 0; kk < m3; ++kk) {
-              float t = 0.f;
-#pragma unroll
-              for (int ch = 0; ch < CPL; ++ch) t = fmaf(x[l1 * l1 + i][ch], h[kk][ch], t);
-#pragma unroll
-              for (int j = 0; j < m2; ++j)
-                dyp[l2 * l2 + j] = fmaf(s_coef[CO + (i * m3 + kk) * m2 + j], t, dyp[l2 * l2 + j]);
-            }
-        }
+          for (int ch = 0; ch < CPL; ++ch) dxl[i][ch] = 0.f;
+        static_for<PS::NP>([&](auto pc) {
+          if constexpr (PS::T.l1[decltype(pc)::value] == decltype(lc)::value)
+            path_adjoint(pc, std::integral_constant<int, 0>{}, xl, dxl, dyp, Grow, grow, dgrow, 1.f);
+        });
+        if (want_dx && active) store_degree<l1, CPL, LAYOUT>(a.grad_features + e * A * C, dxl, C, c0);
       });
-      if (want_dy) {
-        float mine = 0.f;
-#pragma unroll
-        for (int j = 0; j < B; ++j) {
-          const float v = warp_sum(dyp[j]);
-          if (lane == j) mine = v;
-        }
-        if (slices == 1) {
-          if (lane < B) a.grad_harmonics[e * B + lane] = mine;
-        } else {
-          if (lane < B) s_dy[warp * B + lane] = mine;
-          group_barrier(1 + group, 32 * slices);
-          if (s == 0 && lane < B) {
-            float total = 0.f;
-            for (int t = 0; t < slices; ++t) total += s_dy[(warp + t) * B + lane];
-            a.grad_harmonics[e * B + lane] = total;
-          }
-          group_barrier(1 + group, 32 * slices);
-        }
-      }
+      if (want_dy) finish_dy(dyp, e);
       __syncwarp();
+    } else {
+      // Graph: a source node's rows stay in registers while its out-edges are walked.
+      const int64_t k0 = a.offsets[node], k1 = a.offsets[node + 1];
+      float x[A][CPL], dx[A][CPL];
+#pragma unroll
+      for (int r = 0; r < A; ++r)
+#pragma unroll
+        for (int ch = 0; ch < CPL; ++ch) dx[r][ch] = 0.f;
+      load_features<LI, CPL, LAYOUT>(x, a.features + node * A * C, C, c0, active, false);
+      for (int64_t k = k0; k < k1; ++k) {
+        const int64_t e = a.order[k];
+        const int64_t d = a.dst[e];
+        const float m = a.mask ? __ldg(a.mask + e) : 1.f;
+        if (lane < B) s_y[lane] = __ldg(a.harmonics + e * B + lane);
+        __syncwarp();
+        build_bond<PS>(s_coef, s_desc, s_y, s_bond, lane);
+        __syncwarp();
+        float dyp[B];
+#pragma unroll
+        for (int j = 0; j < B; ++j) dyp[j] = 0.f;
+        const float* Grow = a.grad_out + d * (int64_t)PS::ROWS * C;
+        const float* grow = a.gates ? a.gates + e * (int64_t)PS::NP * C : nullptr;
+        float* dgrow = want_dg ? a.grad_gates + e * (int64_t)PS::NP * C : nullptr;
+        static_for<PS::NP>([&](auto pc) {
+          constexpr int l1 = PS::T.l1[decltype(pc)::value];
+          path_adjoint(pc, std::integral_constant<int, l1 * l1>{}, x, dx, dyp, Grow, grow, dgrow, m);
+        });
+        if (want_dy) finish_dy(dyp, e);
+        __syncwarp();
+      }
+      if (want_dx && active) store_features<LI, CPL, LAYOUT>(a.grad_features + node * A * C, dx, C, c0);
     }
-    if (want_dx && active) store_features<LI, CPL, LAYOUT>(a.grad_features + node * A * C, dx, C, c0);
   }
 }
 
 // ---------------------------------------------------------------------------
 // Variant registry (host side)
 // ---------------------------------------------------------------------------
-using KernelFn = void (*)(TPArgs);
-
 enum Kind : int { kForward = 0, kAdjoint = 1, kMessageForward = 2, kMessageAdjoint = 3, kKinds = 4 };
+
+using Launcher = cudaError_t (*)(const TPArgs& args, const float* coef, int grid, int block, size_t smem,
+                                 cudaStream_t stream);
 
 struct Variant {
   int li, le, lo, cpl, layout, kind;
-  KernelFn fn;
+  const void* fn;       // kernel symbol (occupancy queries)
+  Launcher launch;
   int np, bond_width, coef_total, rows, a, b;
   size_t smem;
 };
 
-template <int LI, int LE, int LO, int CPL, int LAYOUT>
-Variant make_variant(int kind, KernelFn fn) {
-  using PS = Paths<LI, LE, LO>;
+template <class PS>
+Variant describe(int cpl, int layout, int kind, int li, int le, int lo) {
   Variant v;
-  v.li = LI; v.le = LE; v.lo = LO; v.cpl = CPL; v.layout = LAYOUT; v.kind = kind; v.fn = fn;
+  v.li = li; v.le = le; v.lo = lo; v.cpl = cpl; v.layout = layout; v.kind = kind;
   v.np = PS::NP; v.bond_width = PS::BW; v.coef_total = PS::CT; v.rows = PS::ROWS; v.a = PS::A; v.b = PS::B;
   v.smem = sizeof(float) * smem_floats<PS>();
+  return v;
+}
+
+template <int LI, int LE, int LO, int CPL, int LAYOUT, int KIND>
+cudaError_t launch_plain(const TPArgs& args, const float*, int grid, int block, size_t smem, cudaStream_t stream) {
+  if constexpr (KIND == kForward)
+    tp_forward_kernel<LI, LE, LO, CPL, LAYOUT><<<grid, block, smem, stream>>>(args);
+  else
+    tp_message_forward_kernel<LI, LE, LO, CPL, LAYOUT><<<grid, block, smem, stream>>>(args);
+  return cudaGetLastError();
+}
+
+template <int LI, int LE, int LO, int CPL, int LAYOUT, bool GRAPH>
+cudaError_t launch_adjoint(const TPArgs& args, const float* coef, int grid, int block, size_t smem,
+                           cudaStream_t stream) {
+  using PS = Paths<LI, LE, LO>;
+  CoefParams<PS::CT> params;
+  params.a = args;
+  for (int t = 0; t < PS::CT; ++t) params.coef[t] = coef[t];
+  tp_adjoint_kernel<LI, LE, LO, CPL, LAYOUT, GRAPH><<<grid, block, smem, stream>>>(params);
+  return cudaGetLastError();
+}
+
+template <int LI, int LE, int LO, int CPL, int LAYOUT, int KIND>
+Variant make_variant() {
+  using PS = Paths<LI, LE, LO>;
+  Variant v = describe<PS>(CPL, LAYOUT, KIND, LI, LE, LO);
+  if constexpr (KIND == kForward) {
+    v.fn = (const void*)tp_forward_kernel<LI, LE, LO, CPL, LAYOUT>;
+    v.launch = launch_plain<LI, LE, LO, CPL, LAYOUT, KIND>;
+  } else if constexpr (KIND == kMessageForward) {
+    v.fn = (const void*)tp_message_forward_kernel<LI, LE, LO, CPL, LAYOUT>;
+    v.launch = launch_plain<LI, LE, LO, CPL, LAYOUT, KIND>;
+  } else {
+    constexpr bool graph = KIND == kMessageAdjoint;
+    v.fn = (const void*)tp_adjoint_kernel<LI, LE, LO, CPL, LAYOUT, graph>;
+    v.launch = launch_adjoint<LI, LE, LO, CPL, LAYOUT, graph>;
+  }
   return v;
 }
 

@@ -7,10 +7,10 @@ namespace ictc {
 
 template <int LI, int LE, int LO, int LAYOUT>
 static void add_message(std::vector<Variant>& out) {
-  out.push_back(make_variant<LI, LE, LO, 1, LAYOUT>(kMessageForward, tp_message_forward_kernel<LI, LE, LO, 1, LAYOUT>));
-  out.push_back(make_variant<LI, LE, LO, 2, LAYOUT>(kMessageForward, tp_message_forward_kernel<LI, LE, LO, 2, LAYOUT>));
-  out.push_back(make_variant<LI, LE, LO, 1, LAYOUT>(kMessageAdjoint, tp_adjoint_kernel<LI, LE, LO, 1, LAYOUT, true>));
-  out.push_back(make_variant<LI, LE, LO, 2, LAYOUT>(kMessageAdjoint, tp_adjoint_kernel<LI, LE, LO, 2, LAYOUT, true>));
+  out.push_back(make_variant<LI, LE, LO, 1, LAYOUT, kMessageForward>());
+  out.push_back(make_variant<LI, LE, LO, 2, LAYOUT, kMessageForward>());
+  out.push_back(make_variant<LI, LE, LO, 1, LAYOUT, kMessageAdjoint>());
+  out.push_back(make_variant<LI, LE, LO, 2, LAYOUT, kMessageAdjoint>());
 }
 
 template <int LI, int LE, int LO>

@@ -7,11 +7,11 @@ namespace ictc {
 
 template <int LI, int LE, int LO, int LAYOUT>
 static void add_standalone(std::vector<Variant>& out) {
-  out.push_back(make_variant<LI, LE, LO, 1, LAYOUT>(kForward, tp_forward_kernel<LI, LE, LO, 1, LAYOUT>));
-  out.push_back(make_variant<LI, LE, LO, 2, LAYOUT>(kForward, tp_forward_kernel<LI, LE, LO, 2, LAYOUT>));
-  out.push_back(make_variant<LI, LE, LO, 4, LAYOUT>(kForward, tp_forward_kernel<LI, LE, LO, 4, LAYOUT>));
-  out.push_back(make_variant<LI, LE, LO, 1, LAYOUT>(kAdjoint, tp_adjoint_kernel<LI, LE, LO, 1, LAYOUT, false>));
-  out.push_back(make_variant<LI, LE, LO, 2, LAYOUT>(kAdjoint, tp_adjoint_kernel<LI, LE, LO, 2, LAYOUT, false>));
+  out.push_back(make_variant<LI, LE, LO, 1, LAYOUT, kForward>());
+  out.push_back(make_variant<LI, LE, LO, 2, LAYOUT, kForward>());
+  out.push_back(make_variant<LI, LE, LO, 4, LAYOUT, kForward>());
+  out.push_back(make_variant<LI, LE, LO, 1, LAYOUT, kAdjoint>());
+  out.push_back(make_variant<LI, LE, LO, 2, LAYOUT, kAdjoint>());
 }
 
 template <int LI, int LE, int LO>
