@@ -1,0 +1,345 @@
+// MACE symmetric contraction on sm_100a, evaluated as a per-node polynomial.
+//
+// The reference recursion (ictc_o3/ops/_mace_symmetric_contraction.py:298-346,
+// with U from ictc_o3/basis/ictd_irreps.py:1465-1517) computes, per node n of
+// species s, channel c and target degree t,
+//   out[m] = sum_nu sum_{i1..inu} U_nu[m, i1..inu, p] W_nu[s, p, c] x_{i1} .. x_{inu}.
+// Symmetrising U over its input axes turns this into a polynomial over the
+// monomials x_i, x_i x_j (i <= j), x_i x_j x_k (i <= j <= k).  The host folds
+// the species weights into one coefficient table (a GEMM, T = Usym W):
+//   T[s][t][row][m][c],  rows in the traversal order
+//     for i: (i) ; for j >= i: (i,j) ; for k >= j: (i,j,k)
+// restricted to the orders present (correlation 1..3).
+//
+// Work decomposition: a warp owns a tile of NB nodes of one species (the host
+// builds species-homogeneous tiles) and a 32-channel slice; lane = channel.
+// Every coefficient row is one coalesced 128-B load reused for the NB nodes.
+// Node inputs are staged in shared memory ([node][d][lane], conflict-free);
+// the feature gradient accumulates in shared memory columns owned by a single
+// lane each, so no atomics are needed.
+#include "ictc_common.cuh"
+#include "ictc_cuda.h"
+
+#include <cstdio>
+
+void ictc_set_error(const char* fmt, const char* detail);
+
+namespace ictc {
+
+constexpr int kScNodes = 4;  // nodes per tile (NB)
+// Warps per CTA: the staged inputs (and gradients) take NB * D * 32 floats per warp.
+__host__ __device__ constexpr int sc_warps(int D) { return D > 9 ? 2 : 4; }
+
+struct SCArgs {
+  const float* __restrict__ x;          // [N, C*D] mul_ir flat
+  const float* __restrict__ table;      // [S, R, C]
+  const int64_t* __restrict__ tiles;    // [num_tiles, NB], -1 padded
+  const int32_t* __restrict__ tile_species;
+  const float* __restrict__ grad_out;   // [N, C*sum_t M_t]
+  float* __restrict__ out;              // [N, C*sum_t M_t]
+  float* __restrict__ grad_x;           // [N, C*D]
+  int64_t num_tiles;
+  int channels;
+  int targets;                          // target_lmax + 1
+  int64_t rows;                         // R (per species)
+};
+
+__host__ __device__ constexpr int sc_monomials(int D, int corr) {
+  int k = 0;
+  if (corr >= 1) k += D;
+  if (corr >= 2) k += D * (D + 1) / 2;
+  if (corr >= 3) k += D * (D + 1) * (D + 2) / 6;
+  return k;
+}
+
+template <int D>
+__device__ __forceinline__ void stage_inputs(const SCArgs& a, float (*s_x)[D][32], const int64_t* nodes, int c,
+                                             bool active) {
+  // s_x[n][d][lane] = x[node][l^2 C + c (2l+1) + i], d = l^2 + i.
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int n = 0; n < kScNodes; ++n) {
+    const int64_t node = nodes[n];
+#pragma unroll
+    for (int l = 0; l * l < D; ++l) {
+      const int m = 2 * l + 1;
+#pragma unroll
+      for (int i = 0; i < m; ++i)
+        s_x[n][l * l + i][lane] =
+            (node >= 0 && active) ? __ldg(a.x + node * (int64_t)a.channels * D + l * l * a.channels + c * m + i) : 0.f;
+    }
+  }
+}
+
+template <int D, int CORR>
+__global__ void __launch_bounds__(128) sc_forward_kernel(SCArgs a) {
+  constexpr int kScWarps = sc_warps(D);
+  __shared__ float s_x_all[kScWarps][kScNodes][D][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float (*s_x)[D][32] = s_x_all[warp];
+  const int C = a.channels;
+  const int slices = (C + 31) / 32;
+  const int64_t units = a.num_tiles * slices;
+  for (int64_t unit = (int64_t)blockIdx.x * kScWarps + warp; unit < units; unit += (int64_t)gridDim.x * kScWarps) {
+    const int64_t tile = unit / slices;
+    const int c = (int)(unit - tile * slices) * 32 + lane;
+    const bool active = c < C;
+    int64_t nodes[kScNodes];
+#pragma unroll
+    for (int n = 0; n < kScNodes; ++n) nodes[n] = a.tiles[tile * kScNodes + n];
+    __syncwarp();
+    stage_inputs<D>(a, s_x, nodes, c, active);
+    __syncwarp();
+    const float* tab = a.table + (int64_t)a.tile_species[tile] * a.rows * C + (active ? c : 0);
+    int64_t out_col = 0;  // first output column of the target block (channels * sum M)
+    for (int t = 0; t < a.targets; ++t) {
+      const int M = 2 * t + 1;
+      float acc[kScNodes][7];
+#pragma unroll
+      for (int n = 0; n < kScNodes; ++n)
+#pragma unroll
+        for (int m = 0; m < 7; ++m) acc[n][m] = 0.f;
+      auto row = [&](const float (&mono)[kScNodes]) {
+#pragma unroll
+        for (int m = 0; m < 7; ++m) {
+          if (m < M) {
+            const float coef = __ldg(tab);
+            tab += C;
+#pragma unroll
+            for (int n = 0; n < kScNodes; ++n) acc[n][m] = fmaf(coef, mono[n], acc[n][m]);
+          }
+        }
+      };
+#pragma unroll 1
+      for (int i = 0; i < D; ++i) {
+        float xi[kScNodes];
+#pragma unroll
+        for (int n = 0; n < kScNodes; ++n) xi[n] = s_x[n][i][lane];
+        if (CORR >= 1) row(xi);
+        if (CORR >= 2) {
+#pragma unroll 1
+          for (int j = i; j < D; ++j) {
+            float xij[kScNodes];
+#pragma unroll
+            for (int n = 0; n < kScNodes; ++n) xij[n] = xi[n] * s_x[n][j][lane];
+            row(xij);
+            if (CORR >= 3) {
+#pragma unroll 1
+              for (int k = j; k < D; ++k) {
+                float xijk[kScNodes];
+#pragma unroll
+                for (int n = 0; n < kScNodes; ++n) xijk[n] = xij[n] * s_x[n][k][lane];
+                row(xijk);
+              }
+            }
+          }
+        }
+      }
+      if (active) {
+#pragma unroll
+        for (int n = 0; n < kScNodes; ++n) {
+          if (nodes[n] < 0) continue;
+          float* dst = a.out + nodes[n] * (int64_t)C * (a.targets * a.targets) + out_col + c * M;
+#pragma unroll
+          for (int m = 0; m < 7; ++m)
+            if (m < M) dst[m] = acc[n][m];
+        }
+      }
+      out_col += (int64_t)C * M;
+    }
+  }
+}
+
+// Feature gradient: dx_i = sum_t sum_m G_t[m] d out_t[m] / d x_i.
+template <int D, int CORR>
+__global__ void __launch_bounds__(128) sc_backward_kernel(SCArgs a) {
+  constexpr int kScWarps = sc_warps(D);
+  __shared__ float s_x_all[kScWarps][kScNodes][D][32];
+  __shared__ float s_dx_all[kScWarps][kScNodes][D][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float (*s_x)[D][32] = s_x_all[warp];
+  float (*s_dx)[D][32] = s_dx_all[warp];
+  const int C = a.channels;
+  const int slices = (C + 31) / 32;
+  const int64_t units = a.num_tiles * slices;
+  const int64_t out_width = (int64_t)C * a.targets * a.targets;
+  for (int64_t unit = (int64_t)blockIdx.x * kScWarps + warp; unit < units; unit += (int64_t)gridDim.x * kScWarps) {
+    const int64_t tile = unit / slices;
+    const int c = (int)(unit - tile * slices) * 32 + lane;
+    const bool active = c < C;
+    int64_t nodes[kScNodes];
+#pragma unroll
+    for (int n = 0; n < kScNodes; ++n) nodes[n] = a.tiles[tile * kScNodes + n];
+    __syncwarp();
+    stage_inputs<D>(a, s_x, nodes, c, active);
+#pragma unroll
+    for (int n = 0; n < kScNodes; ++n)
+#pragma unroll
+      for (int d = 0; d < D; ++d) s_dx[n][d][lane] = 0.f;
+    __syncwarp();
+    const float* tab = a.table + (int64_t)a.tile_species[tile] * a.rows * C + (active ? c : 0);
+    int64_t out_col = 0;
+    for (int t = 0; t < a.targets; ++t) {
+      const int M = 2 * t + 1;
+      float g[kScNodes][7];
+#pragma unroll
+      for (int n = 0; n < kScNodes; ++n)
+#pragma unroll
+        for (int m = 0; m < 7; ++m)
+          g[n][m] = (m < M && nodes[n] >= 0 && active) ? __ldg(a.grad_out + nodes[n] * out_width + out_col + c * M + m)
+                                                       : 0.f;
+      // a[n] = sum_m T[row][m] g[n][m] for the current row
+      auto project = [&](float (&av)[kScNodes]) {
+#pragma unroll
+        for (int n = 0; n < kScNodes; ++n) av[n] = 0.f;
+#pragma unroll
+        for (int m = 0; m < 7; ++m) {
+          if (m < M) {
+            const float coef = __ldg(tab);
+            tab += C;
+#pragma unroll
+            for (int n = 0; n < kScNodes; ++n) av[n] = fmaf(coef, g[n][m], av[n]);
+          }
+        }
+      };
+#pragma unroll 1
+      for (int i = 0; i < D; ++i) {
+        float xi[kScNodes], dxi[kScNodes];
+#pragma unroll
+        for (int n = 0; n < kScNodes; ++n) { xi[n] = s_x[n][i][lane]; dxi[n] = 0.f; }
+        if (CORR >= 1) {
+          float av[kScNodes];
+          project(av);
+#pragma unroll
+          for (int n = 0; n < kScNodes; ++n) dxi[n] += av[n];
+        }
+        if (CORR >= 2) {
+#pragma unroll 1
+          for (int j = i; j < D; ++j) {
+            float xj[kScNodes], dxj[kScNodes];
+#pragma unroll
+            for (int n = 0; n < kScNodes; ++n) { xj[n] = s_x[n][j][lane]; dxj[n] = 0.f; }
+            {
+              // d(x_i x_j): x_j towards i, x_i towards j (both when i == j: 2 x_i).
+              float av[kScNodes];
+              project(av);
+#pragma unroll
+              for (int n = 0; n < kScNodes; ++n) {
+                dxi[n] = fmaf(av[n], xj[n], dxi[n]);
+                dxj[n] = fmaf(av[n], xi[n], dxj[n]);
+              }
+            }
+            if (CORR >= 3) {
+#pragma unroll 1
+              for (int k = j; k < D; ++k) {
+                float av[kScNodes];
+                project(av);
+#pragma unroll
+                for (int n = 0; n < kScNodes; ++n) {
+                  const float xk = s_x[n][k][lane];
+                  dxi[n] = fmaf(av[n], xj[n] * xk, dxi[n]);
+                  dxj[n] = fmaf(av[n], xi[n] * xk, dxj[n]);
+                  s_dx[n][k][lane] = fmaf(av[n], xi[n] * xj[n], s_dx[n][k][lane]);
+                }
+              }
+            }
+#pragma unroll
+            for (int n = 0; n < kScNodes; ++n) s_dx[n][j][lane] += dxj[n];
+          }
+        }
+#pragma unroll
+        for (int n = 0; n < kScNodes; ++n) s_dx[n][i][lane] += dxi[n];
+      }
+      out_col += (int64_t)C * M;
+    }
+    if (active) {
+#pragma unroll
+      for (int n = 0; n < kScNodes; ++n) {
+        if (nodes[n] < 0) continue;
+        float* dst = a.grad_x + nodes[n] * (int64_t)C * D;
+#pragma unroll
+        for (int l = 0; l * l < D; ++l) {
+          const int m = 2 * l + 1;
+#pragma unroll
+          for (int i = 0; i < m; ++i) dst[l * l * C + c * m + i] = s_dx[n][l * l + i][lane];
+        }
+      }
+    }
+    __syncwarp();
+  }
+}
+
+using SCFn = void (*)(SCArgs);
+
+static SCFn sc_kernel(int lmax, int corr, bool backward) {
+#define ICTC_SC_CASE(L, CO)                                                                      \
+  if (lmax == L && corr == CO)                                                                   \
+    return backward ? sc_backward_kernel<(L + 1) * (L + 1), CO> : sc_forward_kernel<(L + 1) * (L + 1), CO>;
+  ICTC_SC_CASE(1, 1) ICTC_SC_CASE(1, 2) ICTC_SC_CASE(1, 3)
+  ICTC_SC_CASE(2, 1) ICTC_SC_CASE(2, 2) ICTC_SC_CASE(2, 3)
+  ICTC_SC_CASE(3, 1) ICTC_SC_CASE(3, 2) ICTC_SC_CASE(3, 3)
+#undef ICTC_SC_CASE
+  return nullptr;
+}
+
+}  // namespace ictc
+
+using namespace ictc;
+
+extern "C" int64_t ictc_sc_table_rows(int lmax, int correlation, int target_lmax) {
+  if (lmax < 0 || correlation < 1 || correlation > 3 || target_lmax < 0) return -1;
+  const int D = (lmax + 1) * (lmax + 1);
+  return (int64_t)sc_monomials(D, correlation) * (target_lmax + 1) * (target_lmax + 1);
+}
+
+extern "C" int ictc_sc_tile_nodes(void) { return kScNodes; }
+
+static int sc_launch(bool backward, const float* x, const float* table, const int64_t* tiles,
+                     const int32_t* tile_species, int64_t num_tiles, const float* grad_out, float* out,
+                     float* grad_x, int channels, int lmax, int correlation, int target_lmax, void* stream) {
+  if (num_tiles < 0 || channels <= 0 || target_lmax < 0 || target_lmax > lmax ||
+      (num_tiles > 0 && (!x || !table || !tiles || !tile_species || (backward ? (!grad_out || !grad_x) : !out)))) {
+    ictc_set_error("ictc_sc: invalid argument%s", "");
+    return ICTC_ERR_INVALID;
+  }
+  SCFn fn = sc_kernel(lmax, correlation, backward);
+  if (!fn) {
+    ictc_set_error("ictc_sc: supported lmax 1..3 and correlation 1..3%s", "");
+    return ICTC_ERR_UNSUPPORTED;
+  }
+  if (num_tiles == 0) return ICTC_OK;
+  SCArgs a{};
+  a.x = x; a.table = table; a.tiles = tiles; a.tile_species = tile_species; a.grad_out = grad_out; a.out = out;
+  a.grad_x = grad_x; a.num_tiles = num_tiles; a.channels = channels; a.targets = target_lmax + 1;
+  a.rows = ictc_sc_table_rows(lmax, correlation, target_lmax);
+  int device = 0, sms = 0, per_sm = 0;
+  cudaGetDevice(&device);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  const int warps = sc_warps((lmax + 1) * (lmax + 1));
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, (const void*)fn, 32 * warps, 0);
+  int64_t units = num_tiles * ((channels + 31) / 32);
+  int64_t blocks = (units + warps - 1) / warps;
+  int64_t cap = (int64_t)sms * (per_sm < 1 ? 1 : per_sm);
+  fn<<<(int)(blocks < cap ? blocks : cap), 32 * warps, 0, (cudaStream_t)stream>>>(a);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) {
+    ictc_set_error("symmetric contraction launch failed: %s", cudaGetErrorString(err));
+    return ICTC_ERR_CUDA;
+  }
+  return ICTC_OK;
+}
+
+extern "C" int ictc_sc_forward(const float* x, const float* table, const int64_t* tiles, const int32_t* tile_species,
+                               int64_t num_tiles, float* out, int channels, int lmax, int correlation,
+                               int target_lmax, void* stream) {
+  return sc_launch(false, x, table, tiles, tile_species, num_tiles, nullptr, out, nullptr, channels, lmax,
+                   correlation, target_lmax, stream);
+}
+
+extern "C" int ictc_sc_backward(const float* x, const float* table, const int64_t* tiles,
+                                const int32_t* tile_species, int64_t num_tiles, const float* grad_out,
+                                float* grad_x, int channels, int lmax, int correlation, int target_lmax,
+                                void* stream) {
+  return sc_launch(true, x, table, tiles, tile_species, num_tiles, grad_out, nullptr, grad_x, channels, lmax,
+                   correlation, target_lmax, stream);
+}

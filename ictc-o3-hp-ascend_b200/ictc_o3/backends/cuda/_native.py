@@ -30,9 +30,13 @@ _SIGNATURES = {
     "ictc_tp_message_forward": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p],
     "ictc_tp_message_backward": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p],
     "ictc_harmonics_table_size": [_i],
+    "ictc_sc_table_rows": [_i, _i, _i],
+    "ictc_sc_tile_nodes": [],
+    "ictc_sc_forward": [_p, _p, _p, _p, _i64, _p, _i, _i, _i, _i, _p],
+    "ictc_sc_backward": [_p, _p, _p, _p, _i64, _p, _p, _i, _i, _i, _i, _p],
     "ictc_direction_harmonics": [_p, _p, _p, _p, _p, _p, _i64, _i, _i, _p],
 }
-_RESTYPES = {"ictc_last_error": ctypes.c_char_p}
+_RESTYPES = {"ictc_last_error": ctypes.c_char_p, "ictc_sc_table_rows": _i64}
 
 _lock = threading.Lock()
 _lib = None

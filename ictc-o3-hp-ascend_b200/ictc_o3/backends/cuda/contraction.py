@@ -1,0 +1,227 @@
+"""Symmetric contraction on the CUDA backend.
+
+Drop-in for ``ictc_o3/backends/ascend/contraction.py`` (``factorized_contractions``).
+For every target degree t the reference recursion
+(``ictc_o3/ops/_mace_symmetric_contraction.py:298-346``)
+
+    out_t[n, c, m] = sum_nu < U_nu[m, i1..inu, :] W_nu[s_n, :, c], x[n, c, i1] .. x[n, c, inu] >
+
+is a polynomial in the node's features.  The host symmetrises U over its input
+axes once (``symmetric_table``), and every call folds the species weights in
+with one GEMM, ``T = Usym W``; the kernel evaluates the polynomial per node.
+Nodes are grouped into species-homogeneous tiles so every coefficient row is
+read once per tile.
+"""
+from __future__ import annotations
+
+import itertools
+from functools import lru_cache
+
+import numpy as np
+import torch
+
+from . import _native
+from ._native import ptr, stream_of
+
+
+# ---------------------------------------------------------------------------
+# Host constants: symmetrised U in the kernel's row order
+# ---------------------------------------------------------------------------
+
+def monomial_rows(dim: int, correlation: int):
+    """Monomials in kernel traversal order: for i: (i); for j>=i: (i,j); for k>=j: (i,j,k)."""
+    rows = []
+    for i in range(dim):
+        if correlation >= 1:
+            rows.append((i,))
+        if correlation >= 2:
+            for j in range(i, dim):
+                rows.append((i, j))
+                if correlation >= 3:
+                    for k in range(j, dim):
+                        rows.append((i, j, k))
+    return rows
+
+
+def symmetric_table(u_tensors, output_l: int, dim: int, correlation: int) -> np.ndarray:
+    """Usym [rows, 2t+1, sum_nu P_nu] with weight columns ordered nu = corr, corr-1, .., 1.
+
+    Row (i, j, k) holds sum over the distinct orderings of (i, j, k) of U_nu[m, ., ., ., p].
+    """
+    M = 2 * output_l + 1
+    blocks = {}
+    for nu in range(1, correlation + 1):
+        u = np.asarray(u_tensors[nu], dtype=np.float64)
+        if output_l == 0:
+            u = u[None]
+        blocks[nu] = u
+    order = list(range(correlation, 0, -1))
+    offsets, total = {}, 0
+    for nu in order:
+        offsets[nu] = total
+        total += blocks[nu].shape[-1]
+    rows = monomial_rows(dim, correlation)
+    table = np.zeros((len(rows), M, total))
+    for r, mono in enumerate(rows):
+        nu = len(mono)
+        u = blocks[nu]
+        acc = np.zeros((M, u.shape[-1]))
+        for perm in set(itertools.permutations(mono)):
+            acc += u[(slice(None),) + perm]
+        table[r, :, offsets[nu]:offsets[nu] + u.shape[-1]] = acc
+    return table
+
+
+@lru_cache(maxsize=None)
+def _table_rows(lmax: int, correlation: int, target_lmax: int) -> int:
+    return int(_native.library().ictc_sc_table_rows(lmax, correlation, target_lmax))
+
+
+# ---------------------------------------------------------------------------
+# Species tiles
+# ---------------------------------------------------------------------------
+
+def species_tiles(index: torch.Tensor, num_elements: int):
+    """Species-homogeneous node tiles [T, NB] (-1 padded) and their species [T] (int32)."""
+    nb = int(_native.library().ictc_sc_tile_nodes())
+    key = (index._version, int(num_elements), nb)
+    cached = getattr(index, "_ictc_cuda_sc_tiles", None)
+    if cached is not None and cached[0] == key:
+        return cached[1]
+    index = index.to(torch.int64)
+    if index.numel():
+        lo, hi = torch.stack((index.min(), index.max())).cpu().tolist()
+        if lo < 0 or hi >= num_elements:
+            raise ValueError("Species index is outside the element table")
+    order = torch.argsort(index, stable=True)
+    counts = torch.bincount(index, minlength=num_elements).cpu().tolist()
+    tiles, species, start = [], [], 0
+    for s, count in enumerate(counts):
+        if count:
+            padded = -(-count // nb) * nb
+            block = torch.full((padded,), -1, dtype=torch.int64, device=index.device)
+            block[:count] = order[start:start + count]
+            tiles.append(block.view(-1, nb))
+            species.append(torch.full((padded // nb,), s, dtype=torch.int32, device=index.device))
+        start += count
+    if tiles:
+        result = (torch.cat(tiles).contiguous(), torch.cat(species).contiguous())
+    else:
+        result = (torch.empty(0, nb, dtype=torch.int64, device=index.device),
+                  torch.empty(0, dtype=torch.int32, device=index.device))
+    index_ref = index
+    try:
+        index_ref._ictc_cuda_sc_tiles = (key, result)
+    except AttributeError:
+        pass
+    return result
+
+
+# ---------------------------------------------------------------------------
+# Autograd
+# ---------------------------------------------------------------------------
+
+class _Contraction(torch.autograd.Function):
+    """out = poly(x; T) for species tiles; x [N, C*D] mul_ir flat, T [S, R, C]."""
+
+    @staticmethod
+    def forward(ctx, spec, tiles, tile_species, x, table):
+        channels, lmax, correlation, target_lmax = spec
+        ctx.spec = spec
+        ctx.save_for_backward(tiles, tile_species, x, table)
+        out = torch.zeros(x.shape[0], channels * (target_lmax + 1) ** 2, device=x.device, dtype=torch.float32)
+        if tiles.shape[0]:
+            _native.call("ictc_sc_forward", ptr(x), ptr(table), ptr(tiles), ptr(tile_species), int(tiles.shape[0]),
+                         ptr(out), channels, lmax, correlation, target_lmax, stream_of(x))
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        tiles, tile_species, x, table = ctx.saved_tensors
+        channels, lmax, correlation, target_lmax = ctx.spec
+        if torch.is_grad_enabled():
+            raise NotImplementedError("second derivatives of the CUDA symmetric contraction are not provided")
+        grad = grad.contiguous()
+        dx = dtable = None
+        if ctx.needs_input_grad[3]:
+            dx = torch.zeros_like(x)
+            if tiles.shape[0]:
+                _native.call("ictc_sc_backward", ptr(x), ptr(table), ptr(tiles), ptr(tile_species),
+                             int(tiles.shape[0]), ptr(grad), ptr(dx), channels, lmax, correlation, target_lmax,
+                             stream_of(x))
+        if ctx.needs_input_grad[4]:
+            dtable = _table_gradient(tiles, tile_species, x, grad, table.shape, ctx.spec)
+        return None, None, None, dx, dtable
+
+
+def _table_gradient(tiles, tile_species, x, grad, shape, spec, chunk=256):
+    """dT[s, row*M + m, c] = sum_{n of species s} G_t[n, c, m] x^{row}[n, c].
+
+    Weight-gradient path (training only), evaluated with batched GEMMs on the
+    device, species by species and in node chunks to bound memory.
+    """
+    channels, lmax, correlation, target_lmax = spec
+    dim = (lmax + 1) ** 2
+    rows = monomial_rows(dim, correlation)
+    n = x.shape[0]
+    feats = torch.cat([x[:, l * l * channels:(l + 1) ** 2 * channels].reshape(n, channels, 2 * l + 1)
+                       for l in range(lmax + 1)], -1)  # [N, C, D]
+    factors = [torch.tensor([mono[a] if a < len(mono) else -1 for mono in rows], device=x.device)
+               for a in range(correlation)]
+    dtable = torch.zeros(shape, device=x.device, dtype=torch.float32)
+    species = tile_species.to(torch.int64)
+    for s in torch.unique(species).tolist():
+        nodes = tiles[species == s].reshape(-1)
+        nodes = nodes[nodes >= 0]
+        for begin in range(0, nodes.numel(), chunk):
+            idx = nodes[begin:begin + chunk]
+            f = feats[idx]                                            # [n, C, D]
+            f1 = torch.cat([f, torch.ones_like(f[:, :, :1])], -1)     # index -1 -> 1
+            mono = torch.ones(idx.numel(), channels, len(rows), device=x.device)
+            for a in range(correlation):
+                mono = mono * f1[:, :, factors[a]]
+            mono_t = mono.permute(1, 2, 0)                            # [C, rows, n]
+            col, row_offset = 0, 0
+            for t in range(target_lmax + 1):
+                M = 2 * t + 1
+                g = grad[idx, col:col + channels * M].reshape(-1, channels, M).permute(1, 0, 2)  # [C, n, M]
+                part = torch.bmm(mono_t, g)                           # [C, rows, M]
+                dtable[s, row_offset:row_offset + len(rows) * M] += part.reshape(channels, -1).t()
+                col += channels * M
+                row_offset += len(rows) * M
+    return dtable
+
+
+# ---------------------------------------------------------------------------
+# Entry point
+# ---------------------------------------------------------------------------
+
+def coefficient_table(owner, device):
+    """T [S, R, C] = Usym W for all targets (differentiable in the weights)."""
+    parts = []
+    for contraction in owner.contractions:
+        usym = contraction.symmetric_table(device)                    # [rows*M, P]
+        weights = contraction.stacked_weights()                       # [S, P, C]
+        parts.append(torch.matmul(usym.unsqueeze(0), weights))        # [S, rows*M, C]
+    return torch.cat(parts, 1).contiguous()
+
+
+def contract_flat(owner, node_feats: torch.Tensor, index: torch.Tensor) -> torch.Tensor:
+    """node_feats [N, C(L+1)^2] mul_ir flat -> [N, C(Lt+1)^2] mul_ir flat."""
+    if node_feats.dtype != torch.float32 or node_feats.device.type != "cuda":
+        raise ValueError("The CUDA symmetric contraction requires CUDA FP32 node features")
+    channels, lmax, corr, target = owner.channels, owner.lmax, owner.correlation, owner.target_lmax
+    table = coefficient_table(owner, node_feats.device)
+    if table.shape[1] != _table_rows(lmax, corr, target):
+        raise ValueError("coefficient table does not match the kernel row count")
+    tiles, tile_species = species_tiles(index.to(node_feats.device), owner.num_elements)
+    spec = (int(channels), int(lmax), int(corr), int(target))
+    return _Contraction.apply(spec, tiles, tile_species, node_feats.contiguous(), table)
+
+
+def factorized_contractions(owner, x: torch.Tensor, index: torch.Tensor) -> torch.Tensor:
+    """Reference signature (``backends/ascend/contraction.py:8``): x [N, C, sum(2l+1)] -> [N, C(Lt+1)^2]."""
+    n, channels = x.shape[0], owner.channels
+    flat = torch.cat([x[:, :, l * l:(l + 1) ** 2].reshape(n, channels * (2 * l + 1))
+                      for l in range(owner.lmax + 1)], -1)
+    return contract_flat(owner, flat, index)

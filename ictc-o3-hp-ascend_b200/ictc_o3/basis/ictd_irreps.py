@@ -322,3 +322,133 @@ def direction_harmonics_all(n: torch.Tensor, lmax: int) -> List[torch.Tensor]:
     from ictc_o3.backends.cuda.geometry import direction_harmonics
     packed = direction_harmonics(n, lmax)
     return [packed[..., l * l:(l + 1) ** 2] for l in range(lmax + 1)]
+
+
+# ---------------------------------------------------------------------------
+# Full SO(3) couplings (any parity) and the MACE-style contraction basis
+# ---------------------------------------------------------------------------
+
+@lru_cache(maxsize=None)
+def monomial_rotation_generator(L: int, axis: str) -> np.ndarray:
+    """Infinitesimal rotation about ``axis`` acting on degree-L monomial coefficients.
+
+    Same convention as ``ictc_o3/basis/ictd_irreps.py:1266-1292``: about z,
+    x^a y^b z^c -> b x^{a+1} y^{b-1} z^c - a x^{a-1} y^{b+1} z^c (cyclic for x, y).
+    """
+    counts = counts_list(L)
+    index = {t: i for i, t in enumerate(counts)}
+    gen = np.zeros((len(counts), len(counts)))
+    for col, (a, b, c) in enumerate(counts):
+        if axis == "x":
+            terms = [(c, (a, b + 1, c - 1)), (-b, (a, b - 1, c + 1))]
+        elif axis == "y":
+            terms = [(a, (a - 1, b, c + 1)), (-c, (a + 1, b, c - 1))]
+        elif axis == "z":
+            terms = [(b, (a + 1, b - 1, c)), (-a, (a - 1, b + 1, c))]
+        else:
+            raise ValueError("axis must be x, y or z")
+        for coef, key in terms:
+            if coef:
+                gen[index[key], col] += coef
+    return gen
+
+
+@lru_cache(maxsize=None)
+def harmonic_rotation_generator(l: int, axis: str) -> torch.Tensor:
+    """The generator restricted to degree-l harmonics: B^T G M B (``ictd_irreps.py:1295-1301``).
+
+    Evaluated with torch float64 in the same association order as the reference,
+    ((B^T G) M) B, so the coupling null vectors below reproduce its bits (their sign
+    choice depends on exact ties between entries of equal magnitude).
+    """
+    B = torch.from_numpy(np.array(harmonic_basis(l)))
+    G = torch.from_numpy(gram_gaussian(l))
+    M = torch.from_numpy(monomial_rotation_generator(l, axis))
+    return (B.T @ G @ M @ B).contiguous()
+
+
+@lru_cache(maxsize=None)
+def build_full_cg_tensor_so3(l1: int, l2: int, l3: int) -> np.ndarray:
+    """Unique SO(3) intertwiner l1 x l2 -> l3 in the ICTC basis, any parity of l1+l2+l3.
+
+    Solves J3 C = C (J1 (x) 1 + 1 (x) J2) for x, y, z generators; the 1-D null space is
+    sign-fixed so that the entry of largest magnitude is positive
+    (``ictc_o3/basis/ictd_irreps.py:1345-1373``).  Shape (2l1+1, 2l2+1, 2l3+1).
+    """
+    d1, d2, d3 = 2 * l1 + 1, 2 * l2 + 1, 2 * l3 + 1
+    if not abs(l1 - l2) <= l3 <= l1 + l2:
+        return np.zeros((d1, d2, d3))
+    eye = lambda n: torch.eye(n, dtype=torch.float64)  # noqa: E731
+    rows = []
+    for axis in ("x", "y", "z"):
+        J1 = harmonic_rotation_generator(l1, axis)
+        J2 = harmonic_rotation_generator(l2, axis)
+        J3 = harmonic_rotation_generator(l3, axis)
+        Jin = torch.kron(J1, eye(d2)) + torch.kron(eye(d1), J2)
+        # Unknown Cmat [d3, d1*d2] (row-major): J3 @ Cmat - Cmat @ Jin = 0.
+        rows.append(torch.kron(J3, eye(d1 * d2)) - torch.kron(eye(d3), Jin.T.contiguous()))
+    A = torch.cat(rows, 0)
+    try:
+        vh = torch.linalg.svd(A)[2]
+    except RuntimeError:  # LAPACK gesdd non-convergence: gesvd through numpy
+        vh = torch.from_numpy(np.linalg.svd(A.numpy(), full_matrices=True)[2])
+    C = vh[-1].reshape(d3, d1 * d2).T.reshape(d1, d2, d3)
+    if C.reshape(-1)[int(C.abs().argmax())] < 0:
+        C = -C
+    return np.ascontiguousarray(C.numpy())
+
+
+def _natural_parity(l: int) -> int:
+    return 1 if l % 2 == 0 else -1
+
+
+@lru_cache(maxsize=None)
+def coupled_basis(lmax: int, correlation: int, irrep_normalization: str = "component", final_l: int = -1):
+    """n-body coupling tensors in the ICTC basis (``ictc_o3/basis/ictd_irreps.py:1389-1446``).
+
+    Returns (l_out, parity, tensor [2l_out+1, D, ..., D]) with D = (lmax+1)^2, built by
+    coupling a left chain with one more input degree at a time and sorting by (l, parity)
+    after every order, as MACE's chained Wigner construction does.  With
+    ``final_l >= 0`` the last order only generates chains ending in degree final_l
+    (the entries a later filter on l_out == final_l keeps, in the same order).
+    """
+    dim = (lmax + 1) ** 2
+    eye = np.eye(dim)
+    basis = [(l, _natural_parity(l), eye[l * l:(l + 1) ** 2]) for l in range(lmax + 1)]
+    for order in range(2, correlation + 1):
+        last = order == correlation and final_l >= 0
+        following = []
+        for l_left, p_left, left in basis:
+            flat_left = left.reshape(2 * l_left + 1, -1)
+            for l_right in range(lmax + 1):
+                for l_out in range(abs(l_left - l_right), l_left + l_right + 1):
+                    if last and l_out != final_l:
+                        continue
+                    cg = apply_cg_normalization(build_full_cg_tensor_so3(l_left, l_right, l_out), l_out,
+                                                irrep_normalization)
+                    coupled = np.einsum("ar,abq->qrb", flat_left, cg)
+                    full = np.zeros((2 * l_out + 1, flat_left.shape[1], dim))
+                    full[:, :, l_right * l_right:(l_right + 1) ** 2] = coupled
+                    following.append((l_out, p_left * _natural_parity(l_right),
+                                      full.reshape(2 * l_out + 1, *left.shape[1:], dim)))
+        basis = sorted(following, key=lambda item: (item[0], item[1]))
+    return basis
+
+
+@lru_cache(maxsize=None)
+def ictd_u_matrix_so3(lmax: int, output_l: int, correlation: int,
+                      irrep_normalization: str = "component") -> np.ndarray:
+    """MACE-style symmetric-contraction U in the ICTC basis (``ictd_irreps.py:1465-1517``).
+
+    Shape [2l+1, D x correlation, P] (leading axis dropped for l = 0), float64.
+    """
+    target = _natural_parity(output_l)
+    tensors = [t for l_out, parity, t in coupled_basis(lmax, correlation, irrep_normalization, output_l)
+               if l_out == output_l and parity == target]
+    dim = (lmax + 1) ** 2
+    if not tensors:
+        shape = ([dim] * correlation + [1]) if output_l == 0 else ([2 * output_l + 1] + [dim] * correlation + [1])
+        return np.zeros(shape)
+    if output_l == 0:
+        tensors = [t[0] for t in tensors]
+    return np.ascontiguousarray(np.stack(tensors, -1))

@@ -172,6 +172,41 @@ def direction_harmonics(directions, lmax, *, policy="auto"):
     return direction_harmonics_all(directions, lmax)
 
 
+def configure_symmetric_contraction(module, *, policy="auto", training=False):
+    """Select the CUDA contraction for a module (reference ``operators.py:189-201``)."""
+    from ictc_o3.ops.symmetric_contraction import ICTDPureUSymmetricContractionSO3
+    if not isinstance(module, ICTDPureUSymmetricContractionSO3):
+        raise TypeError("Expected an ICTC symmetric contraction")
+    if policy not in ("auto", "generated", "reference"):
+        raise ValueError("policy must be auto, generated or reference")
+    require_cuda_fp32(*module.parameters())
+    if module.correlation not in (1, 2, 3):
+        raise ValueError("CUDA symmetric contraction supports correlation 1, 2 and 3")
+    strict_fp32()
+    module._cuda_hp = True
+    return {"backend": "cuda", "selected": "generated"}
+
+
+def create_symmetric_contraction(*, num_elements, lmax, target_lmax=None, channels=64,
+                                 correlation=3, device="cuda", policy="generated", training=False):
+    """Reference ``operators.py:204-218``, CUDA device."""
+    for value, name in ((num_elements, "num_elements"), (channels, "channels"), (correlation, "correlation")):
+        _positive_integer(value, name)
+    if correlation not in (1, 2, 3):
+        raise ValueError("CUDA symmetric contraction supports correlation 1, 2 and 3")
+    _degree(lmax, "lmax")
+    target_lmax = lmax if target_lmax is None else target_lmax
+    _degree(target_lmax, "target_lmax")
+    if torch.device(device).type != "cuda":
+        raise ValueError("This operator factory requires a CUDA device")
+    from ictc_o3.ops.symmetric_contraction import ICTDPureUSymmetricContractionSO3
+    module = ICTDPureUSymmetricContractionSO3(num_elements=num_elements, channels=channels, lmax=lmax,
+                                              target_lmax=target_lmax, correlation=correlation)
+    module = module.to(device=device, dtype=torch.float32)
+    configure_symmetric_contraction(module, policy=policy, training=training)
+    return module
+
+
 def normalized_silu(features, scale=1.):
     require_cuda_fp32(features)
     if not isinstance(scale, (int, float)) or isinstance(scale, bool):
@@ -180,4 +215,4 @@ def normalized_silu(features, scale=1.):
 
 
 __all__ = ["EdgeTensorProduct", "PackedGraphMessage", "GraphMessage", "direction_harmonics",
-           "normalized_silu", "strict_fp32"]
+           "create_symmetric_contraction", "configure_symmetric_contraction", "normalized_silu", "strict_fp32"]

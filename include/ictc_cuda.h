@@ -147,6 +147,33 @@ int ictc_direction_harmonics(const float* directions, const float* table, const 
                              const float* grad_dir, float* out0, float* out1, int64_t rows, int lmax,
                              int mode, void* stream);
 
+/*
+ * MACE symmetric contraction as a per-node polynomial (correlation 1..3,
+ * input degrees 0..lmax with 1 <= lmax <= 3, targets 0..target_lmax <= lmax).
+ *   x      [N, C*(lmax+1)^2]   node features, degree blocks [C][2l+1] (mul_ir)
+ *   table  [S, R, C]           species coefficient table T = Usym * W (host GEMM):
+ *          for each target t, monomial rows in the order
+ *          for i: (i); for j >= i: (i,j); for k >= j: (i,j,k)   (orders <= correlation)
+ *          each row holding 2t+1 consecutive C-vectors; R = ictc_sc_table_rows(...)
+ *   tiles  [num_tiles, ictc_sc_tile_nodes()] node ids of one species each, -1 padded;
+ *          tile_species [num_tiles]
+ *   out    [N, C*(target_lmax+1)^2]  target blocks [C][2t+1] (mul_ir)
+ * Nodes not named by any tile are not written.  Replaces the MACE recursion
+ * (ictc_o3/ops/_mace_symmetric_contraction.py:298-346) and the Ascend factorised
+ * contraction (ictc_o3/backends/ascend/contraction.py:8-45).
+ */
+int64_t ictc_sc_table_rows(int lmax, int correlation, int target_lmax);
+int ictc_sc_tile_nodes(void);
+int ictc_sc_forward(const float* x, const float* table, const int64_t* tiles, const int32_t* tile_species,
+                    int64_t num_tiles, float* out, int channels, int lmax, int correlation, int target_lmax,
+                    void* stream);
+
+/* Feature gradient of ictc_sc_forward for cotangent grad_out: grad_x [N, C*(lmax+1)^2]
+ * (rows of nodes named by a tile are fully written). */
+int ictc_sc_backward(const float* x, const float* table, const int64_t* tiles, const int32_t* tile_species,
+                     int64_t num_tiles, const float* grad_out, float* grad_x, int channels, int lmax,
+                     int correlation, int target_lmax, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,6 +13,10 @@ PyTorch modules on them:
   its VJP (autograd) and the mixed second derivatives (double backward);
 * ``direction_harmonics_all`` (ictc_o3/basis/ictd_irreps.py:1113-1168) with
   first and second derivatives;
+* the full ICTC couplings and the pure-ICTC contraction U tensors
+  (ictc_o3/basis/ictd_irreps.py:1305-1517), pinned through seeded probes, and a
+  symmetric contraction built from those U tensors with the MACE recursion
+  (ictc_o3/ops/_mace_symmetric_contraction.py:298-346);
 * the graph message (gather by src, TP, mask, index_add into dst:
   ictc_o3/backends/ascend/tensor_product.py:189-218 and
   mace_ictc/models/pure_cartesian_ictd_fix.py:1801-1806,1913-1917).
@@ -174,6 +178,86 @@ def message_case(I, name, channels, lmax, nodes, edges, seed):
     print("wrote", name)
 
 
+def full_cg_case(I, name, lmax):
+    """Full SO(3) couplings (any parity) of the ICTC basis (ictd_irreps.py:1305-1373)."""
+    keys, values = [], []
+    for l1 in range(lmax + 1):
+        for l2 in range(lmax + 1):
+            for l3 in range(abs(l1 - l2), l1 + l2 + 1):
+                keys.append((l1, l2, l3))
+                values.append(I.build_full_cg_tensor_so3(l1, l2, l3).numpy().reshape(-1))
+    np.savez_compressed(os.path.join(HERE, name), keys=np.array(keys, dtype=np.int32),
+                        values=np.concatenate(values))
+    print("wrote", name)
+
+
+def u_probe_case(I, name, lmaxes, seed):
+    """Pins ictd_u_matrix_so3 (ictd_irreps.py:1465-1517) by contracting every input
+    axis with a distinct seeded probe vector: result [2t+1, P] per (lmax, t, nu)."""
+    gen = torch.Generator().manual_seed(seed)
+    record = {}
+    for lmax in lmaxes:
+        dim = (lmax + 1) ** 2
+        probes = torch.randn(3, dim, generator=gen, dtype=torch.float64)
+        record[f"probes_l{lmax}"] = probes.numpy()
+        for t in range(lmax + 1):
+            for nu in (1, 2, 3):
+                u = I.ictd_u_matrix_so3(lmax=lmax, output_l=t, correlation=nu, dtype=torch.float64)
+                if t == 0:
+                    u = u.unsqueeze(0)
+                for a in range(nu):
+                    u = torch.tensordot(u, probes[a], dims=([1], [0]))
+                record[f"u_l{lmax}_t{t}_nu{nu}"] = u.numpy()
+    np.savez_compressed(os.path.join(HERE, name), **record)
+    print("wrote", name)
+
+
+def contraction_case(I, name, channels, lmax, target_lmax, correlation, nodes, elements, seed):
+    """Symmetric contraction with the reference's ICTC U tensors and the MACE recursion
+    with element-selected weights (_mace_symmetric_contraction.py:298-346), FP64."""
+    gen = torch.Generator().manual_seed(seed)
+    dim = (lmax + 1) ** 2
+    x = torch.randn(nodes, channels * dim, generator=gen).float()
+    idx = torch.randint(0, elements, (nodes,), generator=gen)
+    record = dict(channels=channels, lmax=lmax, target_lmax=target_lmax, correlation=correlation,
+                  elements=elements, x=x.numpy(), idx=idx.numpy())
+    xd = x.double().requires_grad_(True)
+    blocks = [xd[:, l * l * channels:(l + 1) ** 2 * channels].reshape(nodes, channels, 2 * l + 1)
+              for l in range(lmax + 1)]
+    feats = torch.cat(blocks, -1)
+    outs, weights_all = [], []
+    for t in range(target_lmax + 1):
+        u = {nu: I.ictd_u_matrix_so3(lmax=lmax, output_l=t, correlation=nu, dtype=torch.float64)
+             for nu in range(1, correlation + 1)}
+        ws = {}
+        for nu in range(correlation, 0, -1):
+            p = u[nu].shape[-1]
+            w = (torch.randn(elements, p, channels, generator=gen) / max(p, 1)).float()
+            record[f"w_t{t}_nu{nu}"] = w.numpy()
+            ws[nu] = w.double().requires_grad_(True)
+            weights_all.append(ws[nu])
+
+        def coef(order):
+            sel = ws[order].index_select(0, idx)
+            return torch.tensordot(sel, u[order], dims=([1], [u[order].ndim - 1]))
+        out = coef(correlation)
+        for order in range(correlation - 1, 0, -1):
+            out = torch.einsum("bc...i,bci->bc...", out, feats) + coef(order)
+        out = torch.einsum("bc...i,bci->bc...", out, feats)
+        outs.append(out.reshape(nodes, -1))
+    out = torch.cat(outs, -1)
+    G = torch.randn(out.shape, generator=gen, dtype=torch.float64)
+    grads = torch.autograd.grad((out * G).sum(), [xd] + weights_all)
+    record.update(out64=out.detach().numpy(), G=G.numpy(), dx64=grads[0].numpy())
+    k = 1
+    for t in range(target_lmax + 1):
+        for nu in range(correlation, 0, -1):
+            record[f"dw_t{t}_nu{nu}"] = grads[k].numpy()
+            k += 1
+    np.savez_compressed(os.path.join(HERE, name), **record)
+    print("wrote", name)
+
+
 def main():
     from ictc_o3.basis import ictd_irreps as I
     torch.set_num_threads(max(1, os.cpu_count() or 1))
@@ -185,6 +269,10 @@ def main():
     harmonics_case(I, "harmonics_l6.npz", 6, rows=64, seed=6)
     harmonics_case(I, "harmonics_l3.npz", 3, rows=40, seed=7)
     message_case(I, "message_c32_l2.npz", 32, 2, nodes=14, edges=60, seed=8)
+    full_cg_case(I, "full_cg_l3.npz", 3)
+    u_probe_case(I, "u_probes.npz", (1, 2, 3), seed=9)
+    contraction_case(I, "contraction_c32_l2.npz", 32, 2, 2, 3, nodes=23, elements=3, seed=10)
+    contraction_case(I, "contraction_c32_l1_t0.npz", 32, 1, 0, 2, nodes=9, elements=2, seed=11)
 
 
 if __name__ == "__main__":

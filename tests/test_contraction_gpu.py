@@ -1,0 +1,71 @@
+"""GPU parity of the symmetric-contraction kernels (forward, feature and weight gradients)."""
+import pytest
+import torch
+
+from _util import golden, assert_close
+from oracle import sc_oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _module(g, device):
+    from ictc_o3.ops.symmetric_contraction import ICTDPureUSymmetricContractionSO3
+    C, L, T, corr, S = (int(g[k]) for k in ("channels", "lmax", "target_lmax", "correlation", "elements"))
+    module = ICTDPureUSymmetricContractionSO3(num_elements=S, channels=C, lmax=L, target_lmax=T,
+                                              correlation=corr).to(device)
+    with torch.no_grad():
+        for t, contraction in enumerate(module.contractions):
+            contraction.weights_max.copy_(torch.from_numpy(g[f"w_t{t}_nu{corr}"]))
+            for j, nu in enumerate(range(corr - 1, 0, -1)):
+                contraction.weights[j].copy_(torch.from_numpy(g[f"w_t{t}_nu{nu}"]))
+    return module
+
+
+@pytest.mark.parametrize("name", ["contraction_c32_l2.npz", "contraction_c32_l1_t0.npz"])
+def test_contraction_matches_reference(name, cuda_device):
+    g = golden(name)
+    module = _module(g, cuda_device)
+    x = torch.from_numpy(g["x"]).to(cuda_device).requires_grad_(True)
+    idx = torch.from_numpy(g["idx"]).to(cuda_device)
+    out = module(x, node_type_idx=idx)
+    assert_close(out.detach().cpu(), g["out64"], 1e-5, 1e-3, "contraction forward")
+    G = torch.from_numpy(g["G"]).float().to(cuda_device)
+    params = []
+    corr = int(g["correlation"])
+    for c in module.contractions:
+        params += [c.weights_max, *c.weights]
+    grads = torch.autograd.grad(out, [x] + params, G)
+    assert_close(grads[0].cpu(), g["dx64"], 1e-4, 1e-3, "contraction dx")
+    k = 1
+    for t in range(int(g["target_lmax"]) + 1):
+        for nu in range(corr, 0, -1):
+            assert_close(grads[k].cpu(), g[f"dw_t{t}_nu{nu}"], 1e-4, 1e-3, f"dW t={t} nu={nu}")
+            k += 1
+
+
+@pytest.mark.parametrize("lmax,target,corr", [(1, 1, 3), (2, 2, 3), (2, 0, 3), (3, 3, 3), (2, 2, 2), (3, 1, 1)])
+@pytest.mark.parametrize("channels", [32, 96, 40])
+def test_contraction_random_against_oracle(lmax, target, corr, channels, cuda_device):
+    """Channel tails, partial species tiles, an absent species, every supported degree."""
+    from ictc_o3.ops.symmetric_contraction import ICTDPureUSymmetricContractionSO3
+    torch.manual_seed(lmax * 100 + target * 10 + corr + channels)
+    S, N = 4, 29
+    module = ICTDPureUSymmetricContractionSO3(num_elements=S, channels=channels, lmax=lmax, target_lmax=target,
+                                              correlation=corr).to(cuda_device)
+    x = torch.randn(N, channels * (lmax + 1) ** 2, device=cuda_device)
+    idx = torch.randint(0, S - 1, (N,), device=cuda_device)  # species S-1 never appears
+    xr = x.detach().requires_grad_(True)
+    out = module(xr, node_type_idx=idx)
+    G = torch.randn_like(out)
+    dx = torch.autograd.grad(out, [xr], G)[0]
+    xd = x.double().cpu().requires_grad_(True)
+    feats = sc_oracle.flat_to_mace(xd, channels, lmax)
+    outs = []
+    for t, c in enumerate(module.contractions):
+        u = {nu: c.U_tensors(nu).double().cpu() for nu in range(1, corr + 1)}
+        outs.append(sc_oracle.contraction(u, c.weights_max.detach().double().cpu(),
+                                          [w.detach().double().cpu() for w in c.weights], feats, idx.cpu(), t))
+    ref = torch.cat(outs, -1)
+    (rdx,) = torch.autograd.grad(ref, [xd], G.double().cpu())
+    assert_close(out.detach().cpu(), ref.detach(), 1e-5, 1e-3, "forward")
+    assert_close(dx.cpu(), rdx, 1e-4, 1e-3, "dx")
