@@ -34,9 +34,13 @@ _SIGNATURES = {
     "ictc_sc_tile_nodes": [],
     "ictc_sc_forward": [_p, _p, _p, _p, _i64, _p, _i, _i, _i, _i, _p],
     "ictc_sc_backward": [_p, _p, _p, _p, _i64, _p, _p, _i, _i, _i, _i, _p],
+    "ictc_neighbor_workspace_bytes": [_i64, _p, ctypes.c_float],
+    "ictc_neighbor_count": [_p, _i64, _p, ctypes.c_float, _p, _i64, _p, _p],
+    "ictc_neighbor_fill": [_p, _i64, _p, ctypes.c_float, _p, _i64, _p, _p, _p, _p, _p],
     "ictc_direction_harmonics": [_p, _p, _p, _p, _p, _p, _i64, _i, _i, _p],
 }
-_RESTYPES = {"ictc_last_error": ctypes.c_char_p, "ictc_sc_table_rows": _i64}
+_RESTYPES = {"ictc_last_error": ctypes.c_char_p, "ictc_sc_table_rows": _i64,
+             "ictc_neighbor_workspace_bytes": _i64}
 
 _lock = threading.Lock()
 _lib = None

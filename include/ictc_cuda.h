@@ -174,6 +174,26 @@ int ictc_sc_backward(const float* x, const float* table, const int64_t* tiles, c
                      int64_t num_tiles, const float* grad_out, float* grad_x, int channels, int lmax,
                      int correlation, int target_lmax, void* stream);
 
+/*
+ * Periodic cell-list neighbour search (orthorhombic box, cutoff < L/2, >= 3
+ * cells per axis).  Produces the destination-sorted edge list of the message
+ * kernels: for receiver i, neighbours j with |pos[i] - pos[j] + shift| < cutoff
+ * (minimum image), grouped by i and ordered by neighbour cell then atom id.
+ * Replaces the torch-only radius graph (mace_ictc/utils/graph_utils.py:217-297).
+ *   box: host pointer to the three box lengths.
+ *   workspace: device scratch of ictc_neighbor_workspace_bytes(...) bytes, owned
+ *   by the caller; ictc_neighbor_fill must get the workspace that the preceding
+ *   ictc_neighbor_count on the same stream filled.
+ *   ictc_neighbor_count writes offsets [atoms + 1] (offsets[atoms] = edge count);
+ *   ictc_neighbor_fill writes src [E], dst [E] (int64) and shift [E, 3].
+ */
+int64_t ictc_neighbor_workspace_bytes(int64_t atoms, const float* box, float cutoff);
+int ictc_neighbor_count(const float* pos, int64_t atoms, const float* box, float cutoff, void* workspace,
+                        int64_t workspace_bytes, int64_t* offsets, void* stream);
+int ictc_neighbor_fill(const float* pos, int64_t atoms, const float* box, float cutoff, const void* workspace,
+                       int64_t workspace_bytes, const int64_t* offsets, int64_t* src, int64_t* dst, float* shift,
+                       void* stream);
+
 #ifdef __cplusplus
 }
 #endif
