@@ -280,3 +280,125 @@ extern "C" int ictc_neighbor_fill(const float* pos, int64_t atoms, const float* 
                                                                                    src, dst, shift);
   return check_launch("ictc_neighbor_fill: %s");
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant (no counterpart in the reference).
+//
+// Some callers cannot allocate device memory while they run a step: an MD
+// engine that owns every device buffer through its own pool, a host program
+// linking this C library without a CUDA-aware allocator to hand out scratch, or
+// code that must not call cudaMalloc inside a time-critical loop.  For them the
+// search below keeps its scratch (the cell lists) in a file-scope device array
+// of fixed size, so the caller only provides the outputs.
+// ---------------------------------------------------------------------------
+
+#include <mutex>
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB, held by every GPU that loads the library
+static __device__ __align__(256) unsigned char g_neighbor_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+static std::mutex g_scratch_mutex;
+static void* g_scratch_address[kMaxDevices] = {};
+
+// Device address of g_neighbor_scratch on the current device (host code must not use
+// the symbol's host-side name as a device pointer).  Resolved once per device.
+static int scratch_address(void** out) {
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) {
+    cudaGetLastError();
+    ictc_set_error("ictc_neighbor_list_noalloc: no usable current device%s", "");
+    return ICTC_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (!g_scratch_address[device]) {
+    void* ptr = nullptr;
+    cudaError_t err = cudaGetSymbolAddress(&ptr, g_neighbor_scratch);
+    if (err != cudaSuccess || !ptr) {
+      cudaGetLastError();
+      ictc_set_error("ictc_neighbor_list_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(err));
+      return ICTC_ERR_CUDA;
+    }
+    g_scratch_address[device] = ptr;
+  }
+  *out = g_scratch_address[device];
+  return ICTC_OK;
+}
+
+// Fill phase that writes only when the edge count fits the caller's capacity.
+__global__ void neighbor_fill_capped_kernel(const float* __restrict__ pos, int64_t atoms, CellGrid g,
+                                            NeighborWorkspace ws, const int64_t* __restrict__ offsets,
+                                            int64_t max_edges, int64_t* __restrict__ src, int64_t* __restrict__ dst,
+                                            float* __restrict__ shift) {
+  if (offsets[atoms] > max_edges) return;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < atoms; i += (int64_t)gridDim.x * blockDim.x) {
+    const float px = pos[3 * i], py = pos[3 * i + 1], pz = pos[3 * i + 2];
+    const int cell = ws.cell_of_atom[i];
+    const int cx = cell % g.nx, cy = (cell / g.nx) % g.ny, cz = cell / (g.nx * g.ny);
+    int64_t out = offsets[i];
+    for (int dz = -1; dz <= 1; ++dz) {
+      const int z = (cz + dz + g.nz) % g.nz;
+      for (int dy = -1; dy <= 1; ++dy) {
+        const int y = (cy + dy + g.ny) % g.ny;
+        for (int dx = -1; dx <= 1; ++dx) {
+          const int x = (cx + dx + g.nx) % g.nx;
+          const int c = (z * g.ny + y) * g.nx + x;
+          for (int k = ws.cell_start[c]; k < ws.cell_start[c + 1]; ++k) {
+            const int32_t j = ws.sorted_atoms[k];
+            if (j == i) continue;
+            const float rx = px - pos[3 * j], ry = py - pos[3 * j + 1], rz = pz - pos[3 * j + 2];
+            const float sx = -g.lx * rintf(rx / g.lx), sy = -g.ly * rintf(ry / g.ly), sz = -g.lz * rintf(rz / g.lz);
+            const float vx = rx + sx, vy = ry + sy, vz = rz + sz;
+            if (vx * vx + vy * vy + vz * vz < g.cutoff2) {
+              src[out] = j;
+              dst[out] = i;
+              shift[3 * out] = sx;
+              shift[3 * out + 1] = sy;
+              shift[3 * out + 2] = sz;
+              ++out;
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" int64_t ictc_neighbor_noalloc_scratch_bytes(void) { return (int64_t)kNoAllocScratchBytes; }
+
+extern "C" int ictc_neighbor_list_noalloc(const float* pos, int64_t atoms, const float* box, float cutoff,
+                                          int64_t* offsets, int64_t* src, int64_t* dst, float* shift,
+                                          int64_t max_edges, void* stream) {
+  CellGrid g;
+  if (!box || !make_grid(box, cutoff, &g)) {
+    ictc_set_error("ictc_neighbor_list_noalloc: unsupported box (need cutoff < L/2 and >= 3 cells per axis)%s", "");
+    return ICTC_ERR_UNSUPPORTED;
+  }
+  if (atoms < 0 || atoms > INT32_MAX || !offsets || max_edges < 0 ||
+      (atoms > 0 && (!pos || (max_edges > 0 && (!src || !dst || !shift))))) {
+    ictc_set_error("ictc_neighbor_list_noalloc: invalid argument%s", "");
+    return ICTC_ERR_INVALID;
+  }
+  const size_t need = workspace_layout(atoms, g.cells(), nullptr, nullptr);
+  if (need > kNoAllocScratchBytes) {
+    char msg[160];
+    snprintf(msg, sizeof(msg), "%zu bytes of cell lists exceed the fixed %zu-byte scratch", need,
+             kNoAllocScratchBytes);
+    ictc_set_error("ictc_neighbor_list_noalloc: system too large: %s; use ictc_neighbor_count/fill", msg);
+    return ICTC_ERR_INVALID;
+  }
+  void* scratch = nullptr;
+  int status = scratch_address(&scratch);
+  if (status != ICTC_OK) return status;
+  status = ictc_neighbor_count(pos, atoms, box, cutoff, scratch, (int64_t)kNoAllocScratchBytes, offsets, stream);
+  if (status != ICTC_OK || atoms == 0) return status;
+  NeighborWorkspace ws;
+  workspace_layout(atoms, g.cells(), &ws, (char*)scratch);
+  neighbor_fill_capped_kernel<<<grid_size(atoms, 128), 128, 0, (cudaStream_t)stream>>>(pos, atoms, g, ws, offsets,
+                                                                                         max_edges, src, dst, shift);
+  return check_launch("ictc_neighbor_list_noalloc: %s");
+}

@@ -194,6 +194,29 @@ int ictc_neighbor_fill(const float* pos, int64_t atoms, const float* box, float 
                        int64_t workspace_bytes, const int64_t* offsets, int64_t* src, int64_t* dst, float* shift,
                        void* stream);
 
+/*
+ * Allocation-free neighbour search.  No counterpart in the reference: it exists
+ * for callers that cannot allocate device memory during a step (an MD engine
+ * that owns all device buffers in its own pool, or a host program using this C
+ * library without a CUDA-aware allocator to hand out scratch).
+ * Same result as ictc_neighbor_count followed by ictc_neighbor_fill, but the
+ * cell lists live in a fixed device array inside the library
+ * (ictc_neighbor_noalloc_scratch_bytes() = 8 MiB, kept by every GPU that loads
+ * the library until the process exits; about 650,000 atoms at liquid
+ * densities).  Larger systems are rejected with ICTC_ERR_INVALID before any
+ * work is queued.  The caller passes offsets [atoms + 1] and output buffers of
+ * capacity max_edges; offsets[atoms] always receives the edge count, and the
+ * edges are written only when that count is <= max_edges (read offsets[atoms]
+ * after the stream completes to detect a too-small capacity).  Calls that
+ * overlap on the GPU (other streams or threads) share the array and race;
+ * serialise them.  The first call on a device resolves the array's device
+ * address; make that first call before any stream capture.  Nothing is
+ * allocated or freed.
+ */
+int64_t ictc_neighbor_noalloc_scratch_bytes(void);
+int ictc_neighbor_list_noalloc(const float* pos, int64_t atoms, const float* box, float cutoff, int64_t* offsets,
+                               int64_t* src, int64_t* dst, float* shift, int64_t max_edges, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
