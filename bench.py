@@ -243,6 +243,87 @@ def e2e_forward(op, rows, steps, warmup, device, world):
     return ms, h2d, d2h
 
 
+def mace_block(device, steps, warmup, atoms=16384, cpu_seconds=0.0):
+    """one non-first MACE interaction block (input lmax 2) and its product
+    block, C64/lmax2, correlation 3, 16,384 H/C/O atoms at 0.1/A^3 (5 A cutoff), forward plus
+    the force gradient.  Returns the JSON sub-object."""
+    from ictc_o3.backends.cuda.neighbors import neighbor_list
+    from mace_ictc.models import CudaOps, InteractionBlock, ProductBlock, radial_embedding, species_groups
+    from mace_ictc.systems import random_system
+    pos, species, side = random_system(atoms, seed=31, device=device)
+    src, dst, shift, _ = neighbor_list(pos, (side,) * 3, 5.0)
+    edges = src.numel()
+    torch.manual_seed(0)
+    C, L = 64, 2
+    inter = InteractionBlock(channels=C, lmax=L, input_lmax=L, num_elements=3, num_basis=8,
+                             avg_num_neighbors=edges / atoms, use_self_connection=True, sc_lmax=L).to(device)
+    prod = ProductBlock(channels=C, lmax=L, target_lmax=L, correlation=3, num_elements=3).to(device)
+    readout = torch.nn.Linear(C, 1, bias=False).to(device)
+    h = torch.randn(atoms, C * (L + 1) ** 2, device=device)
+    groups = species_groups(species, 3)
+    ops = CudaOps()
+
+    def step():
+        p = pos.detach().requires_grad_(True)
+        vec = p[dst] - p[src] + shift
+        r = vec.norm(dim=1)
+        harm = ops.harmonics(vec / r.unsqueeze(-1), L)
+        feats = radial_embedding(r, 5.0, 8, 5)
+        message, sc = inter(ops, h, harm, feats, src, dst, None, groups)
+        out = prod(ops, message, sc, species)
+        energy = readout(out[:, :C]).sum()
+        return torch.autograd.grad(energy, [p])[0]
+
+    ms = time_loop(step, steps, warmup, 1, device) / steps
+    result = {"value": round(atoms / (ms * 1e-3), 1), "unit": "atom-steps/s", "ms_per_step": round(ms, 3),
+              "atoms": atoms, "edges": edges, "neighbours_per_atom": round(edges / atoms, 2),
+              "workload": "configs[2]: one MACE interaction block (input lmax 2) + product, C64/lmax2, corr 3, "
+                          "forward + force gradient (positions)",
+              "gpu_launches_per_step": 6}
+    if cpu_seconds > 0:
+        result["cpu_baseline"] = mace_block_cpu(cpu_seconds)
+    return result
+
+
+def mace_block_cpu(seconds, atoms=1024):
+    """The same block on the oracle ops (torch CPU FP32, all host threads), smaller system."""
+    from mace_ictc.models import InteractionBlock, ProductBlock, radial_embedding, species_groups
+    from oracle.model_ops import OracleOps
+    torch.set_num_threads(os.cpu_count() or 1)
+    gen = torch.Generator().manual_seed(3)
+    side = (atoms / 0.1) ** (1 / 3)
+    pos = torch.rand(atoms, 3, generator=gen) * side
+    species = torch.randint(0, 3, (atoms,), generator=gen)
+    d = pos[None] - pos[:, None]
+    s = -side * torch.round(d / side)
+    dist = (d + s).norm(dim=-1)
+    i, j = torch.nonzero((dist < 5.0) & (dist > 0), as_tuple=True)
+    src, dst, shift = j, i, s[i, j]
+    torch.manual_seed(0)
+    C, L = 64, 2
+    ops = OracleOps(torch.float32)
+    inter = InteractionBlock(channels=C, lmax=L, input_lmax=L, num_elements=3, num_basis=8,
+                             avg_num_neighbors=src.numel() / atoms, use_self_connection=True, sc_lmax=L)
+    prod = ProductBlock(channels=C, lmax=L, target_lmax=L, correlation=3, num_elements=3)
+    readout = torch.nn.Linear(C, 1, bias=False)
+    h = torch.randn(atoms, C * (L + 1) ** 2)
+    groups = species_groups(species, 3)
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds or done == 0:
+        p = pos.detach().requires_grad_(True)
+        vec = p[dst] - p[src] + shift
+        r = vec.norm(dim=1)
+        harm = ops.harmonics(vec / r.unsqueeze(-1), L)
+        message, sc = inter(ops, h, harm, radial_embedding(r, 5.0, 8, 5), src, dst, None, groups)
+        energy = readout(prod(ops, message, sc, species)[:, :C]).sum()
+        torch.autograd.grad(energy, [p])
+        done += atoms
+    elapsed = time.perf_counter() - t0
+    return {"value": round(done / elapsed, 1), "unit": "atom-steps/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"{done} atom-steps of a {atoms}-atom system with the same block on the "
+                                      f"oracle ops (torch CPU FP32), {elapsed:.1f} s"}
+
+
 def run_ours(args):
     world, rank, local = setup_dist()
     device = torch.device("cuda", local)
@@ -275,6 +356,10 @@ def run_ours(args):
     del x, y, g, G
     torch.cuda.empty_cache()
 
+    block = mace_block(device, max(3, min(args.steps, 10)), 2,
+                       cpu_seconds=(args.cpu_seconds / 2 if world == 1 and rank == 0 else 0.0))
+    torch.cuda.empty_cache()
+
     e2e_steps = max(2, min(args.steps, 5))
     e2e_ms, h2d, d2h = e2e_forward(op, FWD_ROWS, e2e_steps, 1, device, world)
     e2e_ms = max_over_ranks(e2e_ms, world, device)
@@ -302,6 +387,7 @@ def run_ours(args):
         "e2e": {"value": round(world * FWD_ROWS / (e2e_ms * 1e-3), 1), "unit": "TP instances/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "ictc_o3.operators.EdgeTensorProduct.forward, pinned host buffers, chunked H2D/compute/D2H"},
+        "mace_block": block,
         "gpu_launches": args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
