@@ -35,6 +35,7 @@ def neighbor_list(pos: torch.Tensor, box, cutoff: float):
     src = torch.empty(edges, dtype=torch.int64, device=pos.device)
     dst = torch.empty(edges, dtype=torch.int64, device=pos.device)
     shift = torch.empty(edges, 3, dtype=torch.float32, device=pos.device)
-    _native.call("ictc_neighbor_fill", ptr(pos), int(atoms), box_arr, float(cutoff), ptr(workspace), size,
-                 ptr(offsets), ptr(src), ptr(dst), ptr(shift), stream)
+    if edges:
+        _native.call("ictc_neighbor_fill", ptr(pos), int(atoms), box_arr, float(cutoff), ptr(workspace), size,
+                     ptr(offsets), ptr(src), ptr(dst), ptr(shift), stream)
     return src, dst, shift, offsets

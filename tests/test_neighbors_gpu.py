@@ -16,7 +16,8 @@ def brute(pos, box, cutoff):
 
 
 @pytest.mark.parametrize("atoms,box,cutoff", [(500, (22.0, 17.0, 19.5), 5.0), (4096, (34.4, 34.4, 34.4), 5.0),
-                                              (64, (15.1, 15.1, 15.1), 5.0), (0, (16.0, 16.0, 16.0), 5.0)])
+                                              (64, (15.1, 15.1, 15.1), 5.0), (0, (16.0, 16.0, 16.0), 5.0),
+                                              (30, (40.0, 40.0, 40.0), 0.9)])
 def test_neighbor_list_matches_brute_force(atoms, box, cutoff, cuda_device):
     from ictc_o3.backends.cuda.neighbors import neighbor_list
     gen = torch.Generator(device=cuda_device).manual_seed(atoms)
