@@ -51,6 +51,8 @@ def parse_args():
     p.add_argument("--profile", action="store_true",
                    help="kernel timing only (forward, then forward+VJP) for ncu captures: no e2e, no CPU baseline")
     p.add_argument("--rows", type=int, default=0, help="instances per step in --profile mode (0 = config sizes)")
+    p.add_argument("--profile-block", action="store_true",
+                   help="time only the configs[2] MACE block step (for ncu launch lists)")
     return p.parse_args()
 
 
@@ -493,7 +495,12 @@ def run_profile(args):
 
 def main():
     args = parse_args()
-    if args.profile:
+    if args.profile_block:
+        device = torch.device("cuda", 0)
+        from ictc_o3.backends.cuda import _native
+        _native.library()
+        print(json.dumps({"profile_block": mace_block(device, args.steps, args.warmup)}))
+    elif args.profile:
         run_profile(args)
     elif args.impl == "reference":
         run_reference(args)

@@ -20,6 +20,7 @@ from functools import lru_cache
 import numpy as np
 import torch
 
+from ictc_o3.autograd.adjoint_requirements import required_gradients
 from . import _native
 from ._native import ptr, stream_of
 
@@ -141,15 +142,16 @@ class _Contraction(torch.autograd.Function):
         channels, lmax, correlation, target_lmax = ctx.spec
         if torch.is_grad_enabled():
             raise NotImplementedError("second derivatives of the CUDA symmetric contraction are not provided")
+        need = required_gradients((x, table), ctx.needs_input_grad[3:5])
         grad = grad.contiguous()
         dx = dtable = None
-        if ctx.needs_input_grad[3]:
+        if need[0]:
             dx = torch.zeros_like(x)
             if tiles.shape[0]:
                 _native.call("ictc_sc_backward", ptr(x), ptr(table), ptr(tiles), ptr(tile_species),
                              int(tiles.shape[0]), ptr(grad), ptr(dx), channels, lmax, correlation, target_lmax,
                              stream_of(x))
-        if ctx.needs_input_grad[4]:
+        if need[1]:
             dtable = _table_gradient(tiles, tile_species, x, grad, table.shape, ctx.spec)
         return None, None, None, dx, dtable
 

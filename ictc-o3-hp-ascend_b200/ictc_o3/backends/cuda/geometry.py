@@ -49,7 +49,7 @@ class _Harmonics(torch.autograd.Function):
     @staticmethod
     def backward(ctx, gy):
         (n,) = ctx.saved_tensors
-        if not ctx.needs_input_grad[0]:
+        if not required_gradients((n,), ctx.needs_input_grad[:1])[0]:
             return None, None
         gy = gy.contiguous()
         if torch.is_grad_enabled():
