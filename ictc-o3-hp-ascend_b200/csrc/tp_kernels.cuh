@@ -129,10 +129,25 @@ __global__ void __launch_bounds__(kThreads) tp_message_forward_kernel(TPArgs a) 
 #pragma unroll
       for (int ch = 0; ch < CPL; ++ch) acc[r][ch] = 0.f;
     const int64_t k0 = a.offsets[n], k1 = a.offsets[n + 1];
+    // Edge ids, sources and masks of up to 32 edges are loaded lane-parallel and then
+    // broadcast, so the per-edge loop carries no dependent index loads.
+    int64_t e_lane = 0, s_lane = 0;
+    float m_lane = 1.f;
+    int batch = 0;
     for (int64_t k = k0; k < k1; ++k) {
-      const int64_t e = a.order[k];
-      const int64_t xs = a.src[e];
-      const float m = a.mask ? __ldg(a.mask + e) : 1.f;
+      const int t = (int)((k - k0) & 31);
+      if (t == 0) {
+        const int64_t kl = k + lane;
+        batch = (int)min((int64_t)32, k1 - k);
+        if (lane < batch) {
+          e_lane = a.order ? a.order[kl] : kl;
+          s_lane = a.src[e_lane];
+          m_lane = a.mask ? __ldg(a.mask + e_lane) : 1.f;
+        }
+      }
+      const int64_t e = __shfl_sync(0xffffffffu, e_lane, t);
+      const int64_t xs = __shfl_sync(0xffffffffu, s_lane, t);
+      const float m = __shfl_sync(0xffffffffu, m_lane, t);
       if (lane < B) s_y[lane] = __ldg(a.harmonics + e * B + lane);
       float x[A][CPL];
       load_features<LI, CPL, LAYOUT>(x, a.features + xs * A * C, C, c0, active, false);
@@ -374,10 +389,23 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
 #pragma unroll
         for (int ch = 0; ch < CPL; ++ch) dx[r][ch] = 0.f;
       load_features<LI, CPL, LAYOUT>(x, a.features + node * A * C, C, c0, active, false);
+      int64_t e_lane = 0, d_lane = 0;
+      float m_lane = 1.f;
+      int batch = 0;
       for (int64_t k = k0; k < k1; ++k) {
-        const int64_t e = a.order[k];
-        const int64_t d = a.dst[e];
-        const float m = a.mask ? __ldg(a.mask + e) : 1.f;
+        const int t = (int)((k - k0) & 31);
+        if (t == 0) {
+          const int64_t kl = k + lane;
+          batch = (int)min((int64_t)32, k1 - k);
+          if (lane < batch) {
+            e_lane = a.order ? a.order[kl] : kl;
+            d_lane = a.dst[e_lane];
+            m_lane = a.mask ? __ldg(a.mask + e_lane) : 1.f;
+          }
+        }
+        const int64_t e = __shfl_sync(0xffffffffu, e_lane, t);
+        const int64_t d = __shfl_sync(0xffffffffu, d_lane, t);
+        const float m = __shfl_sync(0xffffffffu, m_lane, t);
         if (lane < B) s_y[lane] = __ldg(a.harmonics + e * B + lane);
         __syncwarp();
         build_bond<PS>(s_coef, s_desc, s_y, s_bond, lane);

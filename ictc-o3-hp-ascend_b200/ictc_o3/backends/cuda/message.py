@@ -40,11 +40,13 @@ class GraphCSR:
 
 
 def _csr(keys: torch.Tensor, nodes: int):
-    order = torch.argsort(keys, stable=True)
+    """(order, offsets); order is None when the edges are already grouped by key."""
     offsets = torch.zeros(nodes + 1, dtype=torch.int64, device=keys.device)
     if keys.numel():
         offsets[1:] = torch.cumsum(torch.bincount(keys, minlength=nodes), 0)
-    return order, offsets
+        if bool((keys[1:] >= keys[:-1]).all()):
+            return None, offsets
+    return torch.argsort(keys, stable=True), offsets
 
 
 def validate_graph(src, dst, src_nodes, dst_nodes, device):

@@ -28,4 +28,14 @@ def random_system(atoms: int, *, density: float = 0.1, min_distance: float = 0.9
     else:
         raise RuntimeError("could not place atoms with the requested minimum distance")
     kinds = torch.randint(0, species, (atoms,), device=device, generator=gen)
-    return pos, kinds, side
+    order = locality_order(pos, side)
+    return pos[order].contiguous(), kinds[order].contiguous(), side
+
+
+def locality_order(pos: torch.Tensor, side: float, cell: float = 5.0) -> torch.Tensor:
+    """Atom permutation sorting atoms by (z, y, x) cell of width ~cell: neighbours then sit
+    close in memory, so gathers of neighbour rows stay in L2."""
+    n = max(1, int(side // cell))
+    idx = torch.clamp((pos / side * n).long(), 0, n - 1)
+    key = (idx[:, 2] * n + idx[:, 1]) * n + idx[:, 0]
+    return torch.argsort(key, stable=True)
