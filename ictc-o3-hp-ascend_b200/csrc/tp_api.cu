@@ -269,7 +269,7 @@ extern "C" int ictc_tp_message_forward(const ictc_tp_plan* plan, const float* no
                                        const float* mask, const int64_t* src, const int64_t* dst_order,
                                        const int64_t* dst_offsets, float* out, int64_t dst_nodes, void* stream) {
   if (!plan || dst_nodes < 0 ||
-      (dst_nodes > 0 && (!node_features || !harmonics || !src || !dst_order || !dst_offsets || !out))) {
+      (dst_nodes > 0 && (!node_features || !harmonics || !src || !dst_offsets || !out))) {
     ictc_set_error("ictc_tp_message_forward: invalid argument%s", "");
     return ICTC_ERR_INVALID;
   }
@@ -286,7 +286,7 @@ extern "C" int ictc_tp_message_backward(const ictc_tp_plan* plan, const float* n
                                         float* grad_node_features, float* grad_harmonics, float* grad_gates,
                                         int64_t src_nodes, void* stream) {
   if (!plan || src_nodes < 0 ||
-      (src_nodes > 0 && (!node_features || !harmonics || !dst || !src_order || !src_offsets || !grad_out))) {
+      (src_nodes > 0 && (!node_features || !harmonics || !dst || !src_offsets || !grad_out))) {
     ictc_set_error("ictc_tp_message_backward: invalid argument%s", "");
     return ICTC_ERR_INVALID;
   }

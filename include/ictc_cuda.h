@@ -97,8 +97,9 @@ int ictc_tp_backward(const ictc_tp_plan* plan, const float* features, const floa
 /*
  * Graph message, out[n] = sum_{e: dst_e = n} mask_e * TP(node_features[src_e],
  * harmonics_e, gates_e * weight) for n < dst_nodes, evaluated over a
- * destination-sorted CSR (dst_order: edge ids grouped by destination,
- * dst_offsets [dst_nodes+1]).  Every output row is written (zero for nodes
+ * destination-sorted CSR (dst_order: edge ids grouped by destination, or NULL
+ * when the edges are already grouped by destination; dst_offsets
+ * [dst_nodes+1]).  Every output row is written (zero for nodes
  * without edges); no atomics.  mask [E] may be NULL.  Indices must be valid
  * (src_e < rows of node_features, dst_e < dst_nodes); the host validates them.
  * Replaces the fused gather / TP / FP32-atomic scatter of `ictc_weighted_map`
@@ -114,8 +115,8 @@ int ictc_tp_message_forward(const ictc_tp_plan* plan, const float* node_features
 
 /*
  * Fused first-order adjoint of ictc_tp_message_forward for cotangent grad_out
- * [dst_nodes, output_width], walked over a source-sorted CSR (src_order,
- * src_offsets [src_nodes+1]).  Writes grad_node_features [src_nodes, ...]
+ * [dst_nodes, output_width], walked over a source-sorted CSR (src_order, or
+ * NULL when the edges are already grouped by source; src_offsets [src_nodes+1]).  Writes grad_node_features [src_nodes, ...]
  * (zero rows for nodes without edges), grad_harmonics [E, B] and grad_gates
  * [E, P*C] (any may be NULL).  Replaces the epilogue adjoints
  * (ictc_o3/ascendc/op_kernel/epilogue.cpp:192 modes 1-2) and the capacity
