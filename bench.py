@@ -53,6 +53,7 @@ def parse_args():
     p.add_argument("--rows", type=int, default=0, help="instances per step in --profile mode (0 = config sizes)")
     p.add_argument("--profile-block", action="store_true",
                    help="time only the configs[2] MACE block step (for ncu launch lists)")
+    p.add_argument("--atoms", type=int, default=16384, help="atoms of the --profile-block system")
     return p.parse_args()
 
 
@@ -499,7 +500,7 @@ def main():
         device = torch.device("cuda", 0)
         from ictc_o3.backends.cuda import _native
         _native.library()
-        print(json.dumps({"profile_block": mace_block(device, args.steps, args.warmup)}))
+        print(json.dumps({"profile_block": mace_block(device, args.steps, args.warmup, atoms=args.atoms)}))
     elif args.profile:
         run_profile(args)
     elif args.impl == "reference":
