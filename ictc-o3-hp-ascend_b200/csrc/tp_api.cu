@@ -105,7 +105,7 @@ extern "C" int ictc_tp_plan_create(int channels, int input_lmax, int edge_lmax, 
   plan->layout = layout;
   const int rows = ref.out_rows;
   const int preferred[kKinds] = {cpl_forward > 0 ? cpl_forward : 4, cpl_backward > 0 ? cpl_backward : 2,
-                                 rows * 2 <= 128 ? 2 : 1, cpl_backward > 0 ? cpl_backward : 2};
+                                 1, cpl_backward > 0 ? cpl_backward : 2};
   for (int kind = 0; kind < kKinds; ++kind) {
     int cpl = pick_cpl(input_lmax, edge_lmax, output_lmax, layout, kind, channels, preferred[kind]);
     plan->v[kind] = cpl ? find_variant(input_lmax, edge_lmax, output_lmax, cpl, layout, kind) : nullptr;

@@ -101,12 +101,15 @@ __global__ void __launch_bounds__(kThreads) tp_forward_kernel(TPArgs a) {
 
 // ---------------------------------------------------------------------------
 // Graph-message forward over a destination CSR: one warp per (destination
-// node, channel slice); the node's whole output row lives in registers.
+// node, channel slice); the node's whole output row lives in registers.  The
+// edge loop is software-pipelined: the next edge's source row, gate row and
+// harmonics are loaded while the current edge is computed, and edge/source ids
+// arrive in lane-parallel batches of 32.
 // ---------------------------------------------------------------------------
 template <int LI, int LE, int LO, int CPL, int LAYOUT>
-__global__ void __launch_bounds__(kThreads) tp_message_forward_kernel(TPArgs a) {
+__global__ void __launch_bounds__(kThreads, (LO >= 3) ? 1 : 2) tp_message_forward_kernel(TPArgs a) {
   using PS = Paths<LI, LE, LO>;
-  constexpr int A = PS::A, B = PS::B, ROWS = PS::ROWS;
+  constexpr int A = PS::A, B = PS::B, ROWS = PS::ROWS, NP = PS::NP;
   extern __shared__ __align__(16) float smem[];
   float* s_coef = smem;
   int2* s_desc = reinterpret_cast<int2*>(smem + round4(PS::CT));
@@ -128,18 +131,26 @@ __global__ void __launch_bounds__(kThreads) tp_message_forward_kernel(TPArgs a) 
     for (int r = 0; r < ROWS; ++r)
 #pragma unroll
       for (int ch = 0; ch < CPL; ++ch) acc[r][ch] = 0.f;
+    float w[NP][CPL];
+#pragma unroll
+    for (int p = 0; p < NP; ++p)
+#pragma unroll
+      for (int ch = 0; ch < CPL; ++ch) w[p][ch] = 1.f;
+    if (a.weight && active) {
+#pragma unroll
+      for (int p = 0; p < NP; ++p) load_vec<CPL>(w[p], a.weight + p * C + c0);
+    }
     const int64_t k0 = a.offsets[n], k1 = a.offsets[n + 1];
-    // Edge ids, sources and masks of up to 32 edges are loaded lane-parallel and then
-    // broadcast, so the per-edge loop carries no dependent index loads.
     int64_t e_lane = 0, s_lane = 0;
     float m_lane = 1.f;
-    int batch = 0;
-    for (int64_t k = k0; k < k1; ++k) {
+    // Registers of the edge being prefetched.
+    float xn[A][CPL], gn[NP][CPL];
+    float yn = 0.f, mn = 1.f;
+    auto fetch = [&](int64_t k) {
       const int t = (int)((k - k0) & 31);
       if (t == 0) {
         const int64_t kl = k + lane;
-        batch = (int)min((int64_t)32, k1 - k);
-        if (lane < batch) {
+        if (kl < k1) {
           e_lane = a.order ? a.order[kl] : kl;
           s_lane = a.src[e_lane];
           m_lane = a.mask ? __ldg(a.mask + e_lane) : 1.f;
@@ -147,36 +158,41 @@ __global__ void __launch_bounds__(kThreads) tp_message_forward_kernel(TPArgs a) 
       }
       const int64_t e = __shfl_sync(0xffffffffu, e_lane, t);
       const int64_t xs = __shfl_sync(0xffffffffu, s_lane, t);
-      const float m = __shfl_sync(0xffffffffu, m_lane, t);
-      if (lane < B) s_y[lane] = __ldg(a.harmonics + e * B + lane);
-      float x[A][CPL];
-      load_features<LI, CPL, LAYOUT>(x, a.features + xs * A * C, C, c0, active, false);
+      mn = __shfl_sync(0xffffffffu, m_lane, t);
+      yn = lane < B ? __ldg(a.harmonics + e * B + lane) : 0.f;
+      load_features<LI, CPL, LAYOUT>(xn, a.features + xs * A * C, C, c0, active, false);
+      const float* grow = a.gates ? a.gates + e * (int64_t)NP * C : nullptr;
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        if (grow && active) load_vec_stream<CPL>(gn[p], grow + p * C + c0);
+        else {
+#pragma unroll
+          for (int ch = 0; ch < CPL; ++ch) gn[p][ch] = 1.f;
+        }
+      }
+    };
+    if (k0 < k1) fetch(k0);
+    for (int64_t k = k0; k < k1; ++k) {
+      float x[A][CPL], g[NP][CPL];
+#pragma unroll
+      for (int r = 0; r < A; ++r)
+#pragma unroll
+        for (int ch = 0; ch < CPL; ++ch) x[r][ch] = xn[r][ch];
+      const float m = mn;
+#pragma unroll
+      for (int p = 0; p < NP; ++p)
+#pragma unroll
+        for (int ch = 0; ch < CPL; ++ch) g[p][ch] = gn[p][ch] * w[p][ch] * m;
+      if (lane < B) s_y[lane] = yn;
+      if (k + 1 < k1) fetch(k + 1);
       __syncwarp();
       build_bond<PS>(s_coef, s_desc, s_y, s_bond, lane);
       __syncwarp();
-      const float* grow = a.gates ? a.gates + e * (int64_t)PS::NP * C : nullptr;
-      static_for<PS::NP>([&](auto pc) {
+      static_for<NP>([&](auto pc) {
         constexpr int p = decltype(pc)::value;
         constexpr int l1 = PS::T.l1[p], l3 = PS::T.l3[p];
         constexpr int m1 = 2 * l1 + 1, m3 = 2 * l3 + 1;
         constexpr int BO = PS::T.bond_off[p], RO = PS::T.out_row[p];
-        float g[CPL];
-#pragma unroll
-        for (int ch = 0; ch < CPL; ++ch) g[ch] = m;
-        if (active) {
-          if (grow) {
-            float t[CPL];
-            load_vec_stream<CPL>(t, grow + p * C + c0);
-#pragma unroll
-            for (int ch = 0; ch < CPL; ++ch) g[ch] *= t[ch];
-          }
-          if (a.weight) {
-            float w[CPL];
-            load_vec<CPL>(w, a.weight + p * C + c0);
-#pragma unroll
-            for (int ch = 0; ch < CPL; ++ch) g[ch] *= w[ch];
-          }
-        }
 #pragma unroll
         for (int kk = 0; kk < m3; ++kk) {
           float base[CPL];
@@ -189,7 +205,7 @@ __global__ void __launch_bounds__(kThreads) tp_message_forward_kernel(TPArgs a) 
             for (int ch = 0; ch < CPL; ++ch) base[ch] = fmaf(b, x[l1 * l1 + i][ch], base[ch]);
           }
 #pragma unroll
-          for (int ch = 0; ch < CPL; ++ch) acc[RO + kk][ch] = fmaf(base[ch], g[ch], acc[RO + kk][ch]);
+          for (int ch = 0; ch < CPL; ++ch) acc[RO + kk][ch] = fmaf(base[ch], g[p][ch], acc[RO + kk][ch]);
         }
       });
       __syncwarp();
@@ -200,7 +216,7 @@ __global__ void __launch_bounds__(kThreads) tp_message_forward_kernel(TPArgs a) 
 #pragma unroll
         for (int r = 0; r < ROWS; ++r) store_vec<CPL>(orow + (int64_t)r * C + c0, acc[r]);
       } else {
-        static_for<PS::NP>([&](auto pc) {
+        static_for<NP>([&](auto pc) {
           constexpr int p = decltype(pc)::value;
           constexpr int m3 = 2 * PS::T.l3[p] + 1;
           constexpr int RO = PS::T.out_row[p];
