@@ -53,7 +53,10 @@ def parse_args():
     p.add_argument("--rows", type=int, default=0, help="instances per step in --profile mode (0 = config sizes)")
     p.add_argument("--profile-block", action="store_true",
                    help="time only the configs[2] MACE block step (for ncu launch lists)")
-    p.add_argument("--atoms", type=int, default=16384, help="atoms of the --profile-block system")
+    p.add_argument("--atoms", type=int, default=0,
+                   help="atoms of the --profile-block (default 16,384) or --profile-md (default 262,144) system")
+    p.add_argument("--profile-md", action="store_true",
+                   help="time only the configs[4] MD step (torchrun for several GPUs)")
     return p.parse_args()
 
 
@@ -327,6 +330,70 @@ def mace_block_cpu(seconds, atoms=1024):
                                       f"oracle ops (torch CPU FP32), {elapsed:.1f} s"}
 
 
+def mace_md(device, world, rank, steps, warmup, atoms=262144, cutoff=5.0):
+    """MACE energy + forces + virial MD step, C64/lmax2, 2 interactions,
+    correlation 3, 262,144 H/C/O atoms at 0.1/A^3, slab-partitioned along x over the ranks
+    with one-cutoff halos.  Every step rebuilds the slab layout and the neighbour lists, then
+    runs the model with the feature halo exchange after layer 1 (and its adjoint) and returns
+    ghost forces to their owners.  Strong scaling: the system size is fixed.
+
+    ``value`` times device-resident positions; ``e2e`` adds, every step, the H2D copy of the
+    positions from pinned host memory and the D2H read of the owned forces, energy and virial."""
+    from mace_ictc.models import MACEICTC
+    from mace_ictc.parallel import distributed_energy_forces, local_positions, slab_edges, slab_layout
+    from mace_ictc.systems import random_system
+    side = (atoms / 0.1) ** (1.0 / 3.0)
+    if rank == 0:
+        pos, species, side0 = random_system(atoms, seed=41, device=device)
+        assert abs(side0 - side) < 1e-9
+    else:
+        pos = torch.empty(atoms, 3, device=device)
+        species = torch.empty(atoms, dtype=torch.int64, device=device)
+    if world > 1:
+        torch.distributed.broadcast(pos, 0)
+        torch.distributed.broadcast(species, 0)
+    torch.manual_seed(0)
+    model = MACEICTC(channels=64, lmax=2, num_interactions=2, correlation=3, r_max=cutoff,
+                     avg_num_neighbors=52.0).to(device)
+    torch.cuda.reset_peak_memory_stats(device)
+    stats = {}
+
+    def step(positions):
+        layout = slab_layout(positions, side, rank, world, cutoff)
+        p = local_positions(layout, positions, side)
+        src, dst, shift = slab_edges(layout, p, side, cutoff, cutoff)
+        stats.update(owned=layout.owned, ghosts=layout.local - layout.owned, edges=int(src.numel()))
+        return distributed_energy_forces(model, layout, p, species.index_select(0, layout.local_global),
+                                         src, dst, shift)
+
+    ms = time_loop(lambda: step(pos), steps, warmup, world, device) / steps
+    ms = max_over_ranks(ms, world, device)
+
+    pos_host = pos.cpu().pin_memory()
+    pos_dev = torch.empty_like(pos)
+    out_host = {}
+
+    def e2e_step():
+        pos_dev.copy_(pos_host, non_blocking=True)
+        energy, forces, virial = step(pos_dev)
+        out_host["forces"] = forces.to("cpu", non_blocking=True)
+        out_host["ev"] = torch.cat([energy, virial]).to("cpu", non_blocking=True)
+
+    e2e_ms = time_loop(e2e_step, max(2, steps // 2), 1, world, device) / max(2, steps // 2)
+    e2e_ms = max_over_ranks(e2e_ms, world, device)
+    peak_gb = max_over_ranks(torch.cuda.max_memory_allocated(device) / 1e9, world, device)
+    ghost_rows = stats["ghosts"]
+    return {"value": round(atoms / (ms * 1e-3), 1), "unit": "atom-steps/s", "ms_per_step": round(ms, 2),
+            "n_gpus": world, "scaling": "strong", "atoms": atoms,
+            "per_rank_rank0": {"owned": stats["owned"], "ghosts": ghost_rows, "edges": stats["edges"]},
+            "halo_bytes_per_exchange_rank0": ghost_rows * 64 * 9 * 4,
+            "peak_device_gb": round(peak_gb, 1),
+            "workload": "configs[4]: MACE C64/lmax2, 2 interactions, corr 3, E+F+virial, neighbour rebuild "
+                        "every step, slab partition along x with 5 A halos, NCCL P2P feature exchange",
+            "e2e": {"value": round(atoms / (e2e_ms * 1e-3), 1), "unit": "atom-steps/s",
+                    "h2d_bytes_per_step": atoms * 12, "d2h_bytes_per_step": stats["owned"] * 12 + 28}}
+
+
 def run_ours(args):
     world, rank, local = setup_dist()
     device = torch.device("cuda", local)
@@ -362,6 +429,8 @@ def run_ours(args):
     block = mace_block(device, max(3, min(args.steps, 10)), 2,
                        cpu_seconds=(args.cpu_seconds / 2 if world == 1 and rank == 0 else 0.0))
     torch.cuda.empty_cache()
+    md = mace_md(device, world, rank, max(3, min(args.steps, 5)), 2)
+    torch.cuda.empty_cache()
 
     e2e_steps = max(2, min(args.steps, 5))
     e2e_ms, h2d, d2h = e2e_forward(op, FWD_ROWS, e2e_steps, 1, device, world)
@@ -391,6 +460,7 @@ def run_ours(args):
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "ictc_o3.operators.EdgeTensorProduct.forward, pinned host buffers, chunked H2D/compute/D2H"},
         "mace_block": block,
+        "mace_md": md,
         "gpu_launches": args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
@@ -500,7 +570,18 @@ def main():
         device = torch.device("cuda", 0)
         from ictc_o3.backends.cuda import _native
         _native.library()
-        print(json.dumps({"profile_block": mace_block(device, args.steps, args.warmup, atoms=args.atoms)}))
+        print(json.dumps({"profile_block": mace_block(device, args.steps, args.warmup, atoms=args.atoms or 16384)}))
+    elif args.profile_md:
+        world, rank, local = setup_dist()
+        device = torch.device("cuda", local)
+        torch.cuda.set_device(device)
+        from ictc_o3.backends.cuda import _native
+        _native.library()
+        md = mace_md(device, world, rank, args.steps, args.warmup, atoms=args.atoms or 262144)
+        if rank == 0:
+            print(json.dumps({"profile_md": md}), flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
     elif args.profile:
         run_profile(args)
     elif args.impl == "reference":

@@ -147,12 +147,14 @@ __global__ void sort_cells_kernel(int64_t cells, NeighborWorkspace ws) {
   }
 }
 
-// Count (FILL = false) or write (FILL = true) the neighbours of every atom.
+// Count (FILL = false) or write (FILL = true) the neighbours of the receivers
+// (atoms [0, receivers)); sources range over all binned atoms.
 template <bool FILL>
-__global__ void neighbor_kernel(const float* __restrict__ pos, int64_t atoms, CellGrid g, NeighborWorkspace ws,
+__global__ void neighbor_kernel(const float* __restrict__ pos, int64_t receivers, CellGrid g, NeighborWorkspace ws,
                                 int32_t* __restrict__ counts, const int64_t* __restrict__ offsets,
                                 int64_t* __restrict__ src, int64_t* __restrict__ dst, float* __restrict__ shift) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < atoms; i += (int64_t)gridDim.x * blockDim.x) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < receivers;
+       i += (int64_t)gridDim.x * blockDim.x) {
     const float px = pos[3 * i], py = pos[3 * i + 1], pz = pos[3 * i + 2];
     const int cell = ws.cell_of_atom[i];
     const int cx = cell % g.nx, cy = (cell / g.nx) % g.ny, cz = cell / (g.nx * g.ny);
@@ -240,16 +242,20 @@ static int prepare(const float* pos, int64_t atoms, const float* box, float cuto
   return ICTC_OK;
 }
 
-extern "C" int ictc_neighbor_count(const float* pos, int64_t atoms, const float* box, float cutoff, void* workspace,
-                                   int64_t workspace_bytes, int64_t* offsets, void* stream) {
+static int neighbor_count(const float* pos, int64_t atoms, int64_t receivers, const float* box, float cutoff,
+                          void* workspace, int64_t workspace_bytes, int64_t* offsets, void* stream, const char* who) {
   CellGrid g;
   NeighborWorkspace ws;
-  int status = prepare(pos, atoms, box, cutoff, workspace, workspace_bytes, offsets, &g, &ws, "ictc_neighbor_count");
+  int status = prepare(pos, atoms, box, cutoff, workspace, workspace_bytes, offsets, &g, &ws, who);
   if (status != ICTC_OK) return status;
+  if (receivers < 0 || receivers > atoms) {
+    ictc_set_error("%s: receivers must lie in [0, atoms]", who);
+    return ICTC_ERR_INVALID;
+  }
   cudaStream_t s = (cudaStream_t)stream;
-  if (atoms == 0) {
+  if (receivers == 0) {
     cudaMemsetAsync(offsets, 0, sizeof(int64_t), s);
-    return check_launch("ictc_neighbor_count: %s");
+    return check_launch("neighbour count: %s");
   }
   const int64_t cells = g.cells();
   cudaMemsetAsync(ws.cell_count, 0, sizeof(int32_t) * cells, s);
@@ -258,27 +264,59 @@ extern "C" int ictc_neighbor_count(const float* pos, int64_t atoms, const float*
   scan_kernel<int32_t, int32_t><<<1, 1024, 0, s>>>(ws.cell_count, ws.cell_start, cells);
   place_kernel<<<grid_size(atoms, 256), 256, 0, s>>>(atoms, ws);
   sort_cells_kernel<<<grid_size(cells, 128), 128, 0, s>>>(cells, ws);
-  neighbor_kernel<false><<<grid_size(atoms, 128), 128, 0, s>>>(pos, atoms, g, ws, ws.atom_count, nullptr, nullptr,
-                                                                nullptr, nullptr);
-  scan_kernel<int32_t, int64_t><<<1, 1024, 0, s>>>(ws.atom_count, offsets, atoms);
-  return check_launch("ictc_neighbor_count: %s");
+  neighbor_kernel<false><<<grid_size(receivers, 128), 128, 0, s>>>(pos, receivers, g, ws, ws.atom_count, nullptr,
+                                                                    nullptr, nullptr, nullptr);
+  scan_kernel<int32_t, int64_t><<<1, 1024, 0, s>>>(ws.atom_count, offsets, receivers);
+  return check_launch("neighbour count: %s");
+}
+
+static int neighbor_fill(const float* pos, int64_t atoms, int64_t receivers, const float* box, float cutoff,
+                         const void* workspace, int64_t workspace_bytes, const int64_t* offsets, int64_t* src,
+                         int64_t* dst, float* shift, void* stream, const char* who) {
+  CellGrid g;
+  NeighborWorkspace ws;
+  int status = prepare(pos, atoms, box, cutoff, workspace, workspace_bytes, offsets, &g, &ws, who);
+  if (status != ICTC_OK) return status;
+  if (receivers < 0 || receivers > atoms) {
+    ictc_set_error("%s: receivers must lie in [0, atoms]", who);
+    return ICTC_ERR_INVALID;
+  }
+  if (receivers == 0) return ICTC_OK;
+  if (!src || !dst || !shift) {
+    ictc_set_error("%s: invalid argument", who);
+    return ICTC_ERR_INVALID;
+  }
+  neighbor_kernel<true><<<grid_size(receivers, 128), 128, 0, (cudaStream_t)stream>>>(pos, receivers, g, ws, nullptr,
+                                                                                       offsets, src, dst, shift);
+  return check_launch("neighbour fill: %s");
+}
+
+extern "C" int ictc_neighbor_count(const float* pos, int64_t atoms, const float* box, float cutoff, void* workspace,
+                                   int64_t workspace_bytes, int64_t* offsets, void* stream) {
+  return neighbor_count(pos, atoms, atoms, box, cutoff, workspace, workspace_bytes, offsets, stream,
+                        "ictc_neighbor_count");
 }
 
 extern "C" int ictc_neighbor_fill(const float* pos, int64_t atoms, const float* box, float cutoff,
                                   const void* workspace, int64_t workspace_bytes, const int64_t* offsets,
                                   int64_t* src, int64_t* dst, float* shift, void* stream) {
-  CellGrid g;
-  NeighborWorkspace ws;
-  int status = prepare(pos, atoms, box, cutoff, workspace, workspace_bytes, offsets, &g, &ws, "ictc_neighbor_fill");
-  if (status != ICTC_OK) return status;
-  if (atoms == 0) return ICTC_OK;
-  if (!src || !dst || !shift) {
-    ictc_set_error("ictc_neighbor_fill: invalid argument%s", "");
-    return ICTC_ERR_INVALID;
-  }
-  neighbor_kernel<true><<<grid_size(atoms, 128), 128, 0, (cudaStream_t)stream>>>(pos, atoms, g, ws, nullptr, offsets,
-                                                                                   src, dst, shift);
-  return check_launch("ictc_neighbor_fill: %s");
+  return neighbor_fill(pos, atoms, atoms, box, cutoff, workspace, workspace_bytes, offsets, src, dst, shift, stream,
+                       "ictc_neighbor_fill");
+}
+
+extern "C" int ictc_neighbor_count_receivers(const float* pos, int64_t atoms, int64_t receivers, const float* box,
+                                             float cutoff, void* workspace, int64_t workspace_bytes,
+                                             int64_t* offsets, void* stream) {
+  return neighbor_count(pos, atoms, receivers, box, cutoff, workspace, workspace_bytes, offsets, stream,
+                        "ictc_neighbor_count_receivers");
+}
+
+extern "C" int ictc_neighbor_fill_receivers(const float* pos, int64_t atoms, int64_t receivers, const float* box,
+                                            float cutoff, const void* workspace, int64_t workspace_bytes,
+                                            const int64_t* offsets, int64_t* src, int64_t* dst, float* shift,
+                                            void* stream) {
+  return neighbor_fill(pos, atoms, receivers, box, cutoff, workspace, workspace_bytes, offsets, src, dst, shift,
+                       stream, "ictc_neighbor_fill_receivers");
 }
 
 // ---------------------------------------------------------------------------

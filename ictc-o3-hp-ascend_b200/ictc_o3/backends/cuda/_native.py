@@ -37,6 +37,8 @@ _SIGNATURES = {
     "ictc_neighbor_workspace_bytes": [_i64, _p, ctypes.c_float],
     "ictc_neighbor_count": [_p, _i64, _p, ctypes.c_float, _p, _i64, _p, _p],
     "ictc_neighbor_fill": [_p, _i64, _p, ctypes.c_float, _p, _i64, _p, _p, _p, _p, _p],
+    "ictc_neighbor_count_receivers": [_p, _i64, _i64, _p, ctypes.c_float, _p, _i64, _p, _p],
+    "ictc_neighbor_fill_receivers": [_p, _i64, _i64, _p, ctypes.c_float, _p, _i64, _p, _p, _p, _p, _p],
     "ictc_neighbor_noalloc_scratch_bytes": [],
     "ictc_neighbor_list_noalloc": [_p, _i64, _p, ctypes.c_float, _p, _p, _p, _p, _i64, _p],
     "ictc_direction_harmonics": [_p, _p, _p, _p, _p, _p, _i64, _i, _i, _p],

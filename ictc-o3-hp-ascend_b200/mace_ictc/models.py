@@ -190,14 +190,16 @@ class InteractionBlock(nn.Module):
         self.message_selector = None if use_self_connection else ElementLinearSO3(num_elements, channels, lmax,
                                                                                   init="identity")
 
-    def forward(self, ops, node_feats, edge_harmonics, edge_feats, src, dst, mask, groups):
+    def forward(self, ops, node_feats, edge_harmonics, edge_feats, src, dst, mask, groups, owned=None):
+        """Messages into the first ``owned`` nodes (all nodes by default); ``groups`` index those."""
+        owned = node_feats.shape[0] if owned is None else owned
         x_up = self.linear_up(node_feats)
         gates = self.fc(edge_feats)
-        msg = ops.message(self.tp, x_up, edge_harmonics, gates, src, dst, mask, node_feats.shape[0])
+        msg = ops.message(self.tp, x_up, edge_harmonics, gates, src, dst, mask, owned)
         message = self.message_linear(msg) / max(self.avg_num_neighbors, 1e-8)
         if self.self_connection is None:
             return self.message_selector(message, groups), None
-        sc_in = node_feats[:, :self.channels * (self.sc_lmax + 1) ** 2]
+        sc_in = node_feats[:owned, :self.channels * (self.sc_lmax + 1) ** 2]
         return message, self.self_connection(sc_in, groups)
 
 
@@ -245,27 +247,53 @@ class MACEICTC(nn.Module):
         self.last_readout = nn.Sequential(nn.Linear(channels, readout_hidden, bias=False), NormalizedSiLU(),
                                           nn.Linear(readout_hidden, 1, bias=False))
 
-    def edge_inputs(self, pos, src, dst, shift_vectors):
+    @staticmethod
+    def edge_vectors(pos, src, dst, shift_vectors=None):
         vec = pos[dst] - pos[src]
-        if shift_vectors is not None:
-            vec = vec + shift_vectors
+        return vec if shift_vectors is None else vec + shift_vectors
+
+    def edge_features(self, vec):
+        """Harmonics, radial embedding and cutoff mask of edge vectors r_e = pos[dst] - pos[src] + shift."""
         length = vec.norm(dim=1)
         n = vec / length.clamp_min(1e-8).unsqueeze(-1)
         harmonics = self.ops.harmonics(n, self.lmax)
         feats = radial_embedding(length, self.r_max, self.num_basis, self.p)
-        mask = (length <= self.r_max).to(pos.dtype).detach()
+        mask = (length <= self.r_max).to(vec.dtype).detach()
         return harmonics, feats, mask
+
+    def edge_inputs(self, pos, src, dst, shift_vectors):
+        return self.edge_features(self.edge_vectors(pos, src, dst, shift_vectors))
 
     def node_energies(self, pos, species, src, dst, shift_vectors=None, layers=None):
         """Per-node energies [N] (sum of the layer readouts)."""
-        groups = species_groups(species, self.num_elements)
-        harmonics, feats, mask = self.edge_inputs(pos, src, dst, shift_vectors)
+        return self.node_energies_from_vectors(self.edge_vectors(pos, src, dst, shift_vectors), species, src, dst,
+                                               layers=layers)
+
+    def node_energies_from_vectors(self, vec, species, src, dst, layers=None, owned=None, exchange=None):
+        """Energies of the first ``owned`` nodes from edge vectors.
+
+        Spatial decomposition (``mace_ictc/interfaces/ascend_lammps.py:286-333``,
+        compact owned outputs): rows ``[0, owned)`` are this rank's atoms and the rest
+        are ghost copies; every edge's receiver ``dst`` is an owned row.  Messages,
+        products and readouts run on owned rows only, and before each later layer
+        ``exchange`` maps the owned features [owned, W] to all local rows (owned rows
+        followed by the ghosts' features from their owners).
+        """
+        n_local = species.shape[0]
+        owned = n_local if owned is None else int(owned)
+        if owned != n_local and exchange is None:
+            raise ValueError("ghost rows need an exchange to refresh their features")
+        own_species = species if owned == n_local else species[:owned]
+        groups = species_groups(own_species, self.num_elements)
+        harmonics, feats, mask = self.edge_features(vec)
         h = self.node_embedding.weight.t().index_select(0, species)
         energy = None
         count = len(self.interactions) if layers is None else layers
         for layer in range(count):
-            message, sc = self.interactions[layer](self.ops, h, harmonics, feats, src, dst, mask, groups)
-            h = self.products[layer](self.ops, message, sc, species)
+            if layer and exchange is not None:
+                h = exchange(h)
+            message, sc = self.interactions[layer](self.ops, h, harmonics, feats, src, dst, mask, groups, owned)
+            h = self.products[layer](self.ops, message, sc, own_species)
             readout = (self.layer_readouts[layer](h[:, :self.channels]) if layer < len(self.interactions) - 1
                        else self.last_readout(h[:, :self.channels]))
             energy = readout if energy is None else energy + readout

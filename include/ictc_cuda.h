@@ -196,6 +196,21 @@ int ictc_neighbor_fill(const float* pos, int64_t atoms, const float* box, float 
                        void* stream);
 
 /*
+ * The same search with receivers restricted to atoms [0, receivers): neighbours
+ * still range over all atoms.  Builds a rank's edges in a spatial decomposition,
+ * where the local atoms are the owned ones followed by ghost copies and only
+ * owned atoms receive messages (the owned-destination edge lists of
+ * mace_ictc/interfaces/ascend_lammps.py:368-421).  offsets has receivers + 1
+ * entries.
+ */
+int ictc_neighbor_count_receivers(const float* pos, int64_t atoms, int64_t receivers, const float* box,
+                                  float cutoff, void* workspace, int64_t workspace_bytes, int64_t* offsets,
+                                  void* stream);
+int ictc_neighbor_fill_receivers(const float* pos, int64_t atoms, int64_t receivers, const float* box,
+                                 float cutoff, const void* workspace, int64_t workspace_bytes,
+                                 const int64_t* offsets, int64_t* src, int64_t* dst, float* shift, void* stream);
+
+/*
  * Allocation-free neighbour search.  No counterpart in the reference: it exists
  * for callers that cannot allocate device memory during a step (an MD engine
  * that owns all device buffers in its own pool, or a host program using this C
