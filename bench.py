@@ -57,6 +57,7 @@ def parse_args():
                    help="atoms of the --profile-block (default 16,384) or --profile-md (default 262,144) system")
     p.add_argument("--profile-md", action="store_true",
                    help="time only the configs[4] MD step (torchrun for several GPUs)")
+    p.add_argument("--profile-train", action="store_true", help="time only the configs[3] training step")
     return p.parse_args()
 
 
@@ -330,6 +331,59 @@ def mace_block_cpu(seconds, atoms=1024):
                                       f"oracle ops (torch CPU FP32), {elapsed:.1f} s"}
 
 
+def mace_train(device, steps, warmup, configs=4, atoms=2048, cutoff=5.0):
+    """force-loss training step of MACE C128/lmax3, 2 interactions,
+    correlation 3.  A batch of 4 periodic configurations of 2,048 H/C/O atoms (0.1/A^3,
+    minimum distance 0.9 A); synthetic targets: per-atom energy N(0,1) and forces N(0,1).
+    loss = mean_c (E_c/N_c - e_c)^2 + 100 mean (F - F_t)^2; each step runs forward, forces
+    with create_graph, the backward through the mixed second derivatives, and an Adam step."""
+    from ictc_o3.backends.cuda.neighbors import neighbor_list
+    from mace_ictc.models import MACEICTC
+    from mace_ictc.systems import random_system
+    pos_l, spec_l, src_l, dst_l, shift_l, batch_l = [], [], [], [], [], []
+    edges = 0
+    for c in range(configs):
+        pos, species, side = random_system(atoms, seed=100 + c, device=device)
+        src, dst, shift, _ = neighbor_list(pos, (side,) * 3, cutoff)
+        pos_l.append(pos)
+        spec_l.append(species)
+        src_l.append(src + c * atoms)
+        dst_l.append(dst + c * atoms)
+        shift_l.append(shift)
+        batch_l.append(torch.full((atoms,), c, dtype=torch.int64, device=device))
+        edges += src.numel()
+    pos, species = torch.cat(pos_l), torch.cat(spec_l)
+    src, dst, shift, batch = torch.cat(src_l), torch.cat(dst_l), torch.cat(shift_l), torch.cat(batch_l)
+    gen = torch.Generator(device=device).manual_seed(77)
+    e_target = torch.randn(configs, device=device, generator=gen)
+    f_target = torch.randn(pos.shape[0], 3, device=device, generator=gen)
+    torch.manual_seed(0)
+    model = MACEICTC(channels=128, lmax=3, num_interactions=2, correlation=3, r_max=cutoff,
+                     avg_num_neighbors=edges / pos.shape[0]).to(device)
+    opt = torch.optim.Adam([p for p in model.parameters() if p.requires_grad], lr=1e-3)
+    torch.cuda.reset_peak_memory_stats(device)
+    losses = []
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        p = pos.detach().requires_grad_(True)
+        energy = model.energy(p, species, src, dst, shift, batch, configs)
+        (grad,) = torch.autograd.grad(energy.sum(), [p], create_graph=True)
+        loss = ((energy / atoms - e_target) ** 2).mean() + 100.0 * ((-grad - f_target) ** 2).mean()
+        loss.backward()
+        opt.step()
+        losses.append(loss.detach())
+
+    ms = time_loop(step, steps, warmup, 1, device) / steps
+    total = configs * atoms
+    return {"value": round(total / (ms * 1e-3), 1), "unit": "atom-steps/s", "ms_per_step": round(ms, 2),
+            "configs_per_s": round(configs / (ms * 1e-3), 2), "atoms": total, "edges": edges,
+            "peak_device_gb": round(torch.cuda.max_memory_allocated(device) / 1e9, 1),
+            "loss_first_last": [round(float(losses[0]), 4), round(float(losses[-1]), 4)],
+            "workload": "configs[3]: MACE C128/lmax3, 2 interactions, corr 3, 4 x 2,048 atoms, "
+                        "loss = E MSE (per atom) + 100 x F MSE, backward through mixed second derivatives, Adam"}
+
+
 def mace_md(device, world, rank, steps, warmup, atoms=262144, cutoff=5.0):
     """MACE energy + forces + virial MD step, C64/lmax2, 2 interactions,
     correlation 3, 262,144 H/C/O atoms at 0.1/A^3, slab-partitioned along x over the ranks
@@ -431,6 +485,8 @@ def run_ours(args):
     torch.cuda.empty_cache()
     md = mace_md(device, world, rank, max(3, min(args.steps, 5)), 2)
     torch.cuda.empty_cache()
+    train = mace_train(device, 3, 2) if world == 1 else None
+    torch.cuda.empty_cache()
 
     e2e_steps = max(2, min(args.steps, 5))
     e2e_ms, h2d, d2h = e2e_forward(op, FWD_ROWS, e2e_steps, 1, device, world)
@@ -461,6 +517,7 @@ def run_ours(args):
                 "api": "ictc_o3.operators.EdgeTensorProduct.forward, pinned host buffers, chunked H2D/compute/D2H"},
         "mace_block": block,
         "mace_md": md,
+        "mace_train": train,
         "gpu_launches": args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
@@ -571,6 +628,11 @@ def main():
         from ictc_o3.backends.cuda import _native
         _native.library()
         print(json.dumps({"profile_block": mace_block(device, args.steps, args.warmup, atoms=args.atoms or 16384)}))
+    elif args.profile_train:
+        device = torch.device("cuda", 0)
+        from ictc_o3.backends.cuda import _native
+        _native.library()
+        print(json.dumps({"profile_train": mace_train(device, args.steps, args.warmup)}), flush=True)
     elif args.profile_md:
         world, rank, local = setup_dist()
         device = torch.device("cuda", local)

@@ -140,9 +140,10 @@ class _Contraction(torch.autograd.Function):
     def backward(ctx, grad):
         tiles, tile_species, x, table = ctx.saved_tensors
         channels, lmax, correlation, target_lmax = ctx.spec
-        if torch.is_grad_enabled():
-            raise NotImplementedError("second derivatives of the CUDA symmetric contraction are not provided")
         need = required_gradients((x, table), ctx.needs_input_grad[3:5])
+        if torch.is_grad_enabled():
+            return (None, None, None) + _differentiable_gradients(tiles, tile_species, x, table, grad, ctx.spec,
+                                                                  need)
         grad = grad.contiguous()
         dx = dtable = None
         if need[0]:
@@ -154,6 +155,60 @@ class _Contraction(torch.autograd.Function):
         if need[1]:
             dtable = _table_gradient(tiles, tile_species, x, grad, table.shape, ctx.spec)
         return None, None, None, dx, dtable
+
+
+def _monomial_factors(dim: int, correlation: int, device):
+    rows = monomial_rows(dim, correlation)
+    return [torch.tensor([mono[a] if a < len(mono) else dim for mono in rows], device=device)
+            for a in range(correlation)], len(rows)
+
+
+def polynomial(x, table, tiles, tile_species, spec):
+    """The contraction as differentiable device tensor algebra (second-order path).
+
+    Same polynomial as the kernels: monomials of each node's features (index ``dim``
+    is the constant 1), contracted with its species' rows of T.  Used only when the
+    gradient itself must be differentiated (force-loss training), where autograd
+    through this expression supplies the mixed second derivatives.
+    """
+    channels, lmax, correlation, target_lmax = spec
+    dim = (lmax + 1) ** 2
+    n = x.shape[0]
+    feats = torch.cat([x[:, l * l * channels:(l + 1) ** 2 * channels].reshape(n, channels, 2 * l + 1)
+                       for l in range(lmax + 1)], -1)
+    f1 = torch.cat([feats, torch.ones_like(feats[:, :, :1])], -1)
+    factors, rows = _monomial_factors(dim, correlation, x.device)
+    species = tile_species.to(torch.int64)
+    blocks = [x.new_zeros(n, channels, 2 * t + 1) for t in range(target_lmax + 1)]
+    for s in torch.unique(species).tolist():
+        nodes = tiles[species == s].reshape(-1)
+        nodes = nodes[nodes >= 0]
+        f = f1.index_select(0, nodes)
+        mono = f[:, :, factors[0]]
+        for a in range(1, correlation):
+            mono = mono * f[:, :, factors[a]]                         # [n_s, C, R]
+        offset = 0
+        for t in range(target_lmax + 1):
+            M = 2 * t + 1
+            coef = table[s, offset:offset + rows * M].reshape(rows, M, channels)
+            blocks[t] = blocks[t].index_copy(0, nodes, torch.einsum("ncr,rmc->ncm", mono, coef))
+            offset += rows * M
+    return torch.cat([b.reshape(n, -1) for b in blocks], -1)
+
+
+def _differentiable_gradients(tiles, tile_species, x, table, grad, spec, need):
+    """(dx, dT) as functions of (x, T, grad) that autograd can differentiate again."""
+    inputs = [t for t, wanted in zip((x, table), need) if wanted]
+    if not inputs:
+        return None, None
+    with torch.enable_grad():
+        out = polynomial(x, table, tiles, tile_species, spec)
+        grads = list(torch.autograd.grad(out, inputs, grad, create_graph=True, allow_unused=True))
+    result = []
+    for t, wanted in zip((x, table), need):
+        g = grads.pop(0) if wanted else None
+        result.append(torch.zeros_like(t) if wanted and g is None else g)
+    return tuple(result)
 
 
 def _table_gradient(tiles, tile_species, x, grad, shape, spec, chunk=256):
@@ -202,8 +257,8 @@ def coefficient_table(owner, device):
     """T [S, R, C] = Usym W for all targets (differentiable in the weights)."""
     parts = []
     for contraction in owner.contractions:
-        usym = contraction.symmetric_table(device)                    # [rows*M, P]
         weights = contraction.stacked_weights()                       # [S, P, C]
+        usym = contraction.symmetric_table(device, weights.dtype)     # [rows*M, P]
         parts.append(torch.matmul(usym.unsqueeze(0), weights))        # [S, rows*M, C]
     return torch.cat(parts, 1).contiguous()
 

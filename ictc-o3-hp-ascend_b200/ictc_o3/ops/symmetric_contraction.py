@@ -48,15 +48,15 @@ class _ICTDPureUContraction(nn.Module):
         """[S, sum P, C], weight columns ordered nu = corr, corr-1, ..., 1."""
         return torch.cat([self.weights_max, *self.weights], 1)
 
-    def symmetric_table(self, device) -> torch.Tensor:
-        """Symmetrised U in the kernel's row order, [rows * (2t+1), sum P] (float32, cached)."""
-        key = str(device)
+    def symmetric_table(self, device, dtype=torch.float32) -> torch.Tensor:
+        """Symmetrised U in the kernel's row order, [rows * (2t+1), sum P] (cached per device, dtype)."""
+        key = (str(device), dtype)
         table = self._table_cache.get(key)
         if table is None:
             from ictc_o3.backends.cuda.contraction import symmetric_table
             dim = self._u64[1].shape[-2]
             sym = symmetric_table(self._u64, self.output_l, dim, self.correlation)
-            table = torch.from_numpy(sym.reshape(-1, sym.shape[-1]).astype(np.float32)).to(device)
+            table = torch.from_numpy(sym.reshape(-1, sym.shape[-1])).to(device=device, dtype=dtype)
             self._table_cache[key] = table
         return table
 

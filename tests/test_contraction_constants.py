@@ -74,3 +74,32 @@ def test_symmetric_table_reproduces_the_polynomial():
                 full = np.tensordot(full, x, axes=([1], [0]))
             np.testing.assert_allclose(got[:, offset:offset + full.shape[-1]], full, rtol=1e-12, atol=1e-12)
             offset += full.shape[-1]
+
+
+@pytest.mark.parametrize("lmax,target,corr", [(2, 2, 3), (1, 0, 2)])
+def test_second_order_polynomial_matches_oracle(lmax, target, corr):
+    """The differentiable polynomial of the second-order path equals the recursion,
+    and so do its first and mixed second derivatives (FP64, CPU)."""
+    from ictc_o3.backends.cuda.contraction import coefficient_table, polynomial, species_tiles
+    from ictc_o3.ops.symmetric_contraction import ICTDPureUSymmetricContractionSO3
+    torch.manual_seed(3)
+    S, N, C = 3, 13, 4
+    module = ICTDPureUSymmetricContractionSO3(num_elements=S, channels=C, lmax=lmax, target_lmax=target,
+                                              correlation=corr).double()
+    x = torch.randn(N, C * (lmax + 1) ** 2, dtype=torch.float64, requires_grad=True)
+    idx = torch.randint(0, S, (N,))
+    table = coefficient_table(module, torch.device("cpu"))
+    tiles, tile_species = species_tiles(idx, S)
+    out = polynomial(x, table.double(), tiles, tile_species, (C, lmax, corr, target))
+    feats = sc_oracle.flat_to_mace(x, C, lmax)
+    ref = torch.cat([sc_oracle.contraction({nu: torch.from_numpy(c._u64[nu]) for nu in range(1, corr + 1)},
+                                           c.weights_max, list(c.weights), feats, idx, t)
+                     for t, c in enumerate(module.contractions)], -1)
+    assert torch.allclose(out, ref, rtol=1e-10, atol=1e-12)
+    G, V = torch.randn_like(out), torch.randn_like(x)
+    (dx,) = torch.autograd.grad(out, [x], G, create_graph=True)
+    (rdx,) = torch.autograd.grad(ref, [x], G, create_graph=True)
+    assert torch.allclose(dx, rdx, rtol=1e-10, atol=1e-12)
+    (h,) = torch.autograd.grad((dx * V).sum(), [x])
+    (rh,) = torch.autograd.grad((rdx * V).sum(), [x])
+    assert torch.allclose(h, rh, rtol=1e-10, atol=1e-12)

@@ -69,3 +69,40 @@ def test_contraction_random_against_oracle(lmax, target, corr, channels, cuda_de
     (rdx,) = torch.autograd.grad(ref, [xd], G.double().cpu())
     assert_close(out.detach().cpu(), ref.detach(), 1e-5, 1e-3, "forward")
     assert_close(dx.cpu(), rdx, 1e-4, 1e-3, "dx")
+
+
+@pytest.mark.parametrize("lmax,target,corr", [(2, 2, 3), (2, 0, 3), (1, 1, 2)])
+def test_contraction_second_derivatives_against_oracle(lmax, target, corr, cuda_device):
+    """Mixed second derivatives (force-loss training): d/d(x, W) of <dx(G), V>."""
+    from ictc_o3.ops.symmetric_contraction import ICTDPureUSymmetricContractionSO3
+    torch.manual_seed(7 + lmax * 10 + target + corr)
+    S, N, channels = 3, 23, 16
+    module = ICTDPureUSymmetricContractionSO3(num_elements=S, channels=channels, lmax=lmax, target_lmax=target,
+                                              correlation=corr).to(cuda_device)
+    params = []
+    for c in module.contractions:
+        params += [c.weights_max, *c.weights]
+    x = torch.randn(N, channels * (lmax + 1) ** 2, device=cuda_device)
+    idx = torch.randint(0, S, (N,), device=cuda_device)
+    xr = x.detach().requires_grad_(True)
+    out = module(xr, node_type_idx=idx)
+    G = torch.randn_like(out)
+    V = torch.randn_like(x)
+    (dx,) = torch.autograd.grad(out, [xr], G, create_graph=True)
+    got = torch.autograd.grad((dx * V).sum(), [xr] + params)
+
+    xd = x.double().cpu().requires_grad_(True)
+    feats = sc_oracle.flat_to_mace(xd, channels, lmax)
+    ref_params, outs = [], []
+    for t, c in enumerate(module.contractions):
+        u = {nu: c.U_tensors(nu).double().cpu() for nu in range(1, corr + 1)}
+        wmax = c.weights_max.detach().double().cpu().requires_grad_(True)
+        ws = [w.detach().double().cpu().requires_grad_(True) for w in c.weights]
+        ref_params += [wmax, *ws]
+        outs.append(sc_oracle.contraction(u, wmax, ws, feats, idx.cpu(), t))
+    ref = torch.cat(outs, -1)
+    (rdx,) = torch.autograd.grad(ref, [xd], G.double().cpu(), create_graph=True)
+    want = torch.autograd.grad((rdx * V.double().cpu()).sum(), [xd] + ref_params)
+    assert_close(dx.detach().cpu(), rdx.detach(), 1e-4, 1e-3, "dx")
+    for k, (a, b) in enumerate(zip(got, want)):
+        assert_close(a.cpu(), b, 1e-4, 1e-3, f"second derivative {k}")

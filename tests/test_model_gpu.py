@@ -93,3 +93,38 @@ def test_forces_are_rotation_covariant_and_match_finite_differences(cuda_device)
         em = oracle.energy(p - dp, species, src, dst, shift)
         fd = -(ep - em) / (2 * h)
         assert abs(float(fd) - float(fo[atom, axis_i])) <= 1e-6 * max(1.0, abs(float(fd)))
+
+
+@pytest.mark.parametrize("lmax", [2, 3])
+def test_force_loss_training_gradients_match_oracle(lmax, cuda_device):
+    """Force-loss training: d(loss)/d(weights) needs the mixed second
+    derivatives of every operator (TP message, harmonics, symmetric contraction)."""
+    pos, species, side = random_system(28, seed=20 + lmax)
+    src, dst, shift = brute_neighbors(pos, side, 5.0)
+    cuda_model, oracle_model = build_models(channels=16, lmax=lmax, seed=9)
+    cuda_model = cuda_model.to(cuda_device)
+    gen = torch.Generator().manual_seed(5)
+    e_target = torch.randn(1, generator=gen, dtype=torch.float64)
+    f_target = torch.randn(pos.shape[0], 3, generator=gen, dtype=torch.float64)
+
+    def loss_of(model, p, sp, s, d, sh, et, ft):
+        p = p.detach().requires_grad_(True)
+        energy = model.energy(p, sp, s, d, sh)
+        (grad,) = torch.autograd.grad(energy.sum(), [p], create_graph=True)
+        return ((energy - et) ** 2).mean() + 100.0 * ((-grad - ft) ** 2).mean()
+
+    dev = cuda_device
+    loss = loss_of(cuda_model, pos.float().to(dev), species.to(dev), src.to(dev), dst.to(dev),
+                   shift.float().to(dev), e_target.float().to(dev), f_target.float().to(dev))
+    names = [n for n, p in cuda_model.named_parameters() if p.requires_grad]
+    got = torch.autograd.grad(loss, [dict(cuda_model.named_parameters())[n] for n in names], allow_unused=True)
+    ref_loss = loss_of(oracle_model, pos, species, src, dst, shift, e_target, f_target)
+    want = torch.autograd.grad(ref_loss, [dict(oracle_model.named_parameters())[n] for n in names],
+                               allow_unused=True)
+    assert_close(loss.detach().cpu(), ref_loss.detach(), 1e-4, None, "loss")
+    for name, a, b in zip(names, got, want):
+        if b is None:
+            assert a is None or float(a.abs().max()) == 0.0, name
+            continue
+        assert a is not None, name
+        assert_close(a.cpu(), b, 1e-4, None, f"d loss / d {name}")
