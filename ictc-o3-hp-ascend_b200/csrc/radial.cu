@@ -1,0 +1,729 @@
+// Fused radial MLP of the MACE interaction on the tensor cores (tcgen05, 3xTF32).
+//
+// The reference's radial network (mace_ictc/models/pure_cartesian_ictd_fix.py:1545-1553,
+// applied per edge at :1787-1800) maps the Bessel x cutoff embedding f [E, F] to the
+// per-edge path gates:
+//     h1 = s*silu(f W1^T), h2 = s*silu(h1 W2^T), h3 = s*silu(h2 W3^T), gates = h3 W4^T
+// with bias-free linears (F -> 64 -> 64 -> 64 -> G) and the normalised SiLU scale s.
+//
+// radial_forward_kernel: one CTA per SM, a tile of 128 edges at a time; the three
+//   hidden layers stay on chip (TMEM accumulators, shared-memory operands) and only
+//   the gates are written.  W4's rows are split into column groups so that one group
+//   plus the hidden weights fit in shared memory; each group recomputes the (cheap)
+//   hidden layers.
+// radial_w4_adjoint_kernel: dh3 = dgates W4, a streaming GEMM over K = G with a
+//   4-stage cp.async pipeline (dgates from HBM, W4^T chunks from L2).
+// radial_chain_kernel: recomputes the hidden layers, keeps s*silu'(a_l) in TMEM and
+//   runs the chain dh3 -> da3 -> dh2 -> ... -> df.
+//
+// Every product is 3xTF32 (A_hi B_hi + A_hi B_lo + A_lo B_hi with hi = TF32
+// rounding of the value and lo = the FP32 remainder): relative error ~1e-6, the
+// FP32 contract of the reference.  Weights arrive pre-split and pre-swizzled in
+// one image (ictc_radial_pack) so kernels copy them flat.
+#include <cstring>
+#include <mutex>
+
+#include "ictc_common.cuh"
+#include "ictc_cuda.h"
+#include "tc_sm100.cuh"
+
+void ictc_set_error(const char* fmt, const char* detail);
+
+namespace ictc {
+namespace {
+
+using namespace tc;
+
+constexpr int kHidden = 64;
+constexpr int kMaxFeatures = 8;
+constexpr int kTile = 128;             // edges per tile = MMA M
+constexpr int kThreads = 128;          // thread r owns tile row r (TMEM lane r)
+constexpr float kSiluScale = 1.6791767923989418f;
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s: far above any legitimate wait
+
+// Image layout (bytes).  Square hidden weights: hi [2 atoms][64 rows][128 B], lo after.
+constexpr uint32_t kSquare = 2 * 2 * kHidden * kAtomBytes;        // 32,768
+constexpr uint32_t kW1 = kHidden * kAtomBytes;                    // 8,192: hi k0-7, lo k8-15 per row
+constexpr uint32_t kW1T = 2 * 2 * 16 * kAtomBytes;                // 8,192: N = 16 (F padded)
+constexpr uint32_t kOffW1 = 0, kOffW2 = kOffW1 + kW1, kOffW3 = kOffW2 + kSquare, kOffW3T = kOffW3 + kSquare,
+                   kOffW2T = kOffW3T + kSquare, kOffW1T = kOffW2T + kSquare, kOffW4 = kOffW1T + kW1T;
+constexpr uint32_t kHiddenImage = kOffW4;                         // 147,456: W1..W1T
+
+struct RadialShape {
+  int features, gates, nc, groups, chunks;
+  uint64_t w4, w4t, total;
+};
+
+bool radial_shape(int features, int hidden, int gates, RadialShape* s) {
+  if (features < 1 || features > kMaxFeatures || hidden != kHidden || gates < 32 || gates % 32) return false;
+  s->features = features;
+  s->gates = gates;
+  s->nc = 0;
+  for (int nc : {176, 160, 128, 96, 64, 32})
+    if (gates % nc == 0) {
+      s->nc = nc;
+      break;
+    }
+  s->groups = gates / s->nc;
+  s->chunks = gates / 32;
+  s->w4 = kOffW4;
+  s->w4t = s->w4 + (uint64_t)gates * 512u;
+  s->total = s->w4t + (uint64_t)gates * 512u;
+  return true;
+}
+
+struct RadialArgs {
+  const unsigned char* image;
+  const float* feats;        // [E, F]
+  const float* grad_gates;   // [E, G]
+  const float* grad_h3;      // [E, 64]
+  float* gates;              // [E, G]
+  float* out_h3;             // [E, 64]
+  float* grad_feats;         // [E, F]
+  int* status;
+  int64_t edges;
+  int features, gates_width, nc, groups, chunks;
+};
+
+__device__ __forceinline__ void flag_error(int* status, int code) {
+  if (status) atomicExch(status, code);
+}
+
+__device__ __forceinline__ float silu_scaled(float a) { return kSiluScale * a / (1.0f + __expf(-a)); }
+__device__ __forceinline__ float silu_scaled_grad(float a) {
+  const float sig = 1.0f / (1.0f + __expf(-a));
+  return kSiluScale * sig * (1.0f + a * (1.0f - sig));
+}
+
+// Flat copy of `bytes` (multiple of 16) from global to shared memory by the block.
+__device__ __forceinline__ void copy_flat(unsigned char* dst, const unsigned char* src, uint32_t bytes) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+  uint4* d = reinterpret_cast<uint4*>(dst);
+  for (uint32_t i = threadIdx.x; i < bytes / 16; i += blockDim.x) d[i] = __ldg(s + i);
+}
+
+// Write 16 consecutive K values (k0 .. k0+15, k0 % 16 == 0) of row r into a [128 x 64]
+// hi/lo operand (hi atoms at `hi`, lo atoms at hi + 32 KB).
+__device__ __forceinline__ void put_operand16(unsigned char* hi, uint32_t r, uint32_t k0, const float* v) {
+  const uint32_t atom = k0 / kAtomK, chunk0 = (k0 % kAtomK) / 4;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float4 h, l;
+    h.x = tf32_hi(v[4 * q + 0]); l.x = v[4 * q + 0] - h.x;
+    h.y = tf32_hi(v[4 * q + 1]); l.y = v[4 * q + 1] - h.y;
+    h.z = tf32_hi(v[4 * q + 2]); l.z = v[4 * q + 2] - h.z;
+    h.w = tf32_hi(v[4 * q + 3]); l.w = v[4 * q + 3] - h.w;
+    const uint32_t off = atom * kTile * kAtomBytes + sw128_chunk(r, chunk0 + q);
+    *reinterpret_cast<float4*>(hi + off) = h;
+    *reinterpret_cast<float4*>(hi + 2 * kTile * kAtomBytes + off) = l;
+  }
+}
+
+// Feature row (F <= 8 values) as the layer-1 operand: chunks 0-1 hi, 2-3 lo.
+__device__ __forceinline__ void put_features(unsigned char* hbuf, const RadialArgs& a, int64_t e, uint32_t r) {
+  float f[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = (e < a.edges && i < a.features) ? __ldg(a.feats + e * a.features + i) : 0.f;
+  float hv[8], lv[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    hv[i] = tf32_hi(f[i]);
+    lv[i] = f[i] - hv[i];
+  }
+  *reinterpret_cast<float4*>(hbuf + sw128_chunk(r, 0)) = make_float4(hv[0], hv[1], hv[2], hv[3]);
+  *reinterpret_cast<float4*>(hbuf + sw128_chunk(r, 1)) = make_float4(hv[4], hv[5], hv[6], hv[7]);
+  *reinterpret_cast<float4*>(hbuf + sw128_chunk(r, 2)) = make_float4(lv[0], lv[1], lv[2], lv[3]);
+  *reinterpret_cast<float4*>(hbuf + sw128_chunk(r, 3)) = make_float4(lv[4], lv[5], lv[6], lv[7]);
+}
+
+// D = A[128 x 64] * B[N x 64]^T for a hi/lo operand at `a` (lo +32 KB) and a weight
+// image at `b` with `rows` rows (lo at + 2 * rows * 128).
+__device__ __forceinline__ void gemm_k64(uint32_t d, uint32_t a, uint32_t b, uint32_t rows, uint32_t idesc) {
+#pragma unroll
+  for (uint32_t kk = 0; kk < 8; ++kk) {
+    const uint32_t ao = (kk / 4) * kTile * kAtomBytes + (kk % 4) * 32;
+    const uint32_t bo = (kk / 4) * rows * kAtomBytes + (kk % 4) * 32;
+    mma_tf32x3(d, a + ao, a + 2 * kTile * kAtomBytes + ao, b + bo, b + 2 * rows * kAtomBytes + bo, idesc,
+               kk > 0 ? 1u : 0u);
+  }
+}
+
+// Layer 1 (K = F <= 8 padded to one K step): operand and weights keep hi at
+// k 0-7 and lo at k 8-15 of the same rows.
+__device__ __forceinline__ void gemm_layer1(uint32_t d, uint32_t a, uint32_t b) {
+  mma_tf32x3(d, a, a + 32, b, b + 32, idesc_tf32(kTile, kHidden), 0u);
+}
+
+// Block-wide agreement after a wait: every thread learns whether all succeeded.
+__device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t& phase, int* status) {
+  const bool ok = mbar_wait(bar, phase, kWaitNs);
+  phase ^= 1u;
+  const bool all = __syncthreads_and(ok) != 0;
+  if (!all && threadIdx.x == 0) flag_error(status, 1);
+  fence_after_sync();
+  return all;
+}
+
+__device__ __forceinline__ unsigned char* aligned_smem(unsigned char* raw) {
+  return reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+}
+
+// ---------------------------------------------------------------------------
+// Forward
+// ---------------------------------------------------------------------------
+
+template <int NC>
+__global__ void __launch_bounds__(kThreads, 1) radial_forward_kernel(RadialArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = aligned_smem(smem_raw);
+  constexpr uint32_t kSW4 = kOffW3T;                 // W1, W2, W3 occupy [0, kOffW3T)
+  constexpr uint32_t kSH = kSW4 + NC * 512;          // hidden operand, 64 KB
+  constexpr uint32_t kSBar = kSH + 65536;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kSBar);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + kSBar + 8);
+
+  const int group = blockIdx.x % a.groups;
+  const int first = blockIdx.x / a.groups, stride = gridDim.x / a.groups;
+  copy_flat(smem, a.image, kOffW3T);
+  copy_flat(smem + kSW4, a.image + kOffW4 + (uint64_t)group * NC * 512, NC * 512);
+  if (threadIdx.x == 0) mbar_init(bar, 1);
+  if (threadIdx.x < 32) tmem_alloc(slot, 256);
+  fence_async_smem();
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = *slot;
+  const uint32_t lane = (threadIdx.x / 32) * 32;
+  const uint32_t base = smem_u32(smem);
+  const uint32_t r = threadIdx.x;
+  uint32_t phase = 0;
+  const int64_t tiles = (a.edges + kTile - 1) / kTile;
+
+  for (int64_t t = first; t < tiles; t += stride) {
+    const int64_t e = t * kTile + r;
+    put_features(smem + kSH, a, e, r);
+    fence_async_smem();
+    __syncthreads();
+    if (r == 0) {
+      fence_after_sync();
+      gemm_layer1(tmem, base + kSH, base + kOffW1);
+      mma_commit(bar);
+    }
+    bool ok = wait_all(bar, phase, a.status);
+    for (int layer = 0; ok && layer < 3; ++layer) {
+      // Epilogue: h = s * silu(D) into the operand buffer.
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float v[16];
+        tmem_load16(tmem + (lane << 16) + 16 * q, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = silu_scaled(v[i]);
+        put_operand16(smem + kSH, r, 16 * q, v);
+      }
+      fence_async_smem();
+      fence_before_sync();
+      __syncthreads();
+      if (r == 0) {
+        fence_after_sync();
+        if (layer < 2) {
+          gemm_k64(tmem, base + kSH, base + (layer == 0 ? kOffW2 : kOffW3), kHidden, idesc_tf32(kTile, kHidden));
+        } else {
+          gemm_k64(tmem + 64, base + kSH, base + kSW4, NC, idesc_tf32(kTile, NC));
+        }
+        mma_commit(bar);
+      }
+      ok = wait_all(bar, phase, a.status);
+    }
+    if (!ok) break;
+    // Gates of this column group: row r, columns [group*NC, group*NC + NC).
+#pragma unroll 1
+    for (int q = 0; q < NC / 16; ++q) {
+      float v[16];
+      tmem_load16(tmem + (lane << 16) + 64 + 16 * q, v);
+      if (e < a.edges) {
+        float4* dst = reinterpret_cast<float4*>(a.gates + e * a.gates_width + group * NC + 16 * q);
+        dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+        dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+        dst[2] = make_float4(v[8], v[9], v[10], v[11]);
+        dst[3] = make_float4(v[12], v[13], v[14], v[15]);
+      }
+    }
+    fence_before_sync();
+    __syncthreads();
+  }
+  fence_before_sync();
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    fence_after_sync();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dh3 = dgates W4 (K = G streamed in chunks of 32)
+// ---------------------------------------------------------------------------
+
+constexpr int kStages = 4;
+constexpr uint32_t kStageBytes = 3 * 16384;  // A hi, A lo, B (W4^T chunk hi+lo)
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void issue_chunk(const RadialArgs& a, uint32_t stage, int64_t tile, int chunk) {
+  // A: rows of dgates, 32 values (8 x 16 B) per row, swizzled into the A-hi buffer.
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t idx = threadIdx.x + kThreads * i;
+    const uint32_t r = idx / 8, ch = idx % 8;
+    const int64_t e = tile * kTile + r;
+    const bool valid = e < a.edges;
+    const float* src = valid ? a.grad_gates + e * a.gates_width + chunk * 32 + ch * 4 : a.grad_gates;
+    cp_async16(stage + sw128_chunk(r, ch), src, valid ? 16u : 0u);
+  }
+  // B: the chunk's W4^T image (hi 8 KB, lo 8 KB), flat.
+  const unsigned char* img = a.image + kOffW4 + (uint64_t)a.gates_width * 512u + (uint64_t)chunk * 16384u;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t idx = threadIdx.x + kThreads * i;
+    cp_async16(stage + 2 * 16384 + idx * 16, img + idx * 16, 16u);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) radial_w4_adjoint_kernel(RadialArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = aligned_smem(smem_raw);
+  constexpr uint32_t kSBar = kStages * kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSBar);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + kSBar + 8 * kStages);
+  if (threadIdx.x == 0)
+    for (int s = 0; s < kStages; ++s) mbar_init(bars + s, 1);
+  if (threadIdx.x < 32) tmem_alloc(slot, 64);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = *slot;
+  const uint32_t lane = (threadIdx.x / 32) * 32;
+  const uint32_t base = smem_u32(smem);
+  const uint32_t r = threadIdx.x;
+  const int64_t tiles = (a.edges + kTile - 1) / kTile;
+  const int chunks = a.chunks;
+  // Flattened (tile, chunk) sequence of this CTA.
+  const int64_t my_tiles = tiles > blockIdx.x ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int64_t total = my_tiles * chunks;
+  uint32_t phases = 0, pending = 0;
+  auto item_tile = [&](int64_t q) { return blockIdx.x + (q / chunks) * gridDim.x; };
+  bool ok = true;
+
+  for (int64_t q = 0; q < kStages - 1; ++q) {
+    if (q < total) issue_chunk(a, base + (uint32_t)(q % kStages) * kStageBytes, item_tile(q), (int)(q % chunks));
+    cp_async_commit();
+  }
+  for (int64_t q = 0; q < total && ok; ++q) {
+    const uint32_t s = (uint32_t)(q % kStages);
+    const int chunk = (int)(q % chunks);
+    // Refill the stage read by MMA q-1 with item q + kStages - 1 once that MMA is done.
+    const int64_t next = q + kStages - 1;
+    if (next < total) {
+      const uint32_t ns = (uint32_t)(next % kStages);
+      if (pending & (1u << ns)) {
+        const bool done = mbar_wait(bars + ns, (phases >> ns) & 1u, kWaitNs);
+        phases ^= 1u << ns;
+        pending &= ~(1u << ns);
+        if (__syncthreads_and(done) == 0) {
+          if (threadIdx.x == 0) flag_error(a.status, 2);
+          ok = false;
+          break;
+        }
+      }
+      issue_chunk(a, base + ns * kStageBytes, item_tile(next), (int)(next % chunks));
+    }
+    cp_async_commit();
+    cp_async_wait<kStages - 1>();
+    __syncthreads();
+    // Split A in place: hi (TF32-rounded) stays, lo goes to the A-lo buffer.
+    unsigned char* st = smem + s * kStageBytes;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t off = (threadIdx.x + kThreads * i) * 16;
+      float4 v = *reinterpret_cast<float4*>(st + off);
+      float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
+      *reinterpret_cast<float4*>(st + off) = h;
+      *reinterpret_cast<float4*>(st + 16384 + off) = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+    }
+    fence_async_smem();
+    fence_before_sync();
+    __syncthreads();
+    if (r == 0) {
+      fence_after_sync();
+      const uint32_t sa = base + s * kStageBytes;
+#pragma unroll
+      for (uint32_t kk = 0; kk < 4; ++kk)
+        mma_tf32x3(tmem, sa + kk * 32, sa + 16384 + kk * 32, sa + 32768 + kk * 32, sa + 32768 + 8192 + kk * 32,
+                   idesc_tf32(kTile, kHidden), (chunk > 0 || kk > 0) ? 1u : 0u);
+      mma_commit(bars + s);
+    }
+    pending |= 1u << s;
+    if (chunk == chunks - 1) {
+      // Tile done: wait for its last MMA, then write dh3.
+      const bool done = mbar_wait(bars + s, (phases >> s) & 1u, kWaitNs);
+      phases ^= 1u << s;
+      pending &= ~(1u << s);
+      if (__syncthreads_and(done) == 0) {
+        if (threadIdx.x == 0) flag_error(a.status, 3);
+        ok = false;
+        break;
+      }
+      fence_after_sync();
+      const int64_t e = item_tile(q) * kTile + r;
+#pragma unroll
+      for (int qq = 0; qq < 4; ++qq) {
+        float v[16];
+        tmem_load16(tmem + (lane << 16) + 16 * qq, v);
+        if (e < a.edges) {
+          float4* dst = reinterpret_cast<float4*>(a.out_h3 + e * kHidden + 16 * qq);
+          dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+          dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+          dst[2] = make_float4(v[8], v[9], v[10], v[11]);
+          dst[3] = make_float4(v[12], v[13], v[14], v[15]);
+        }
+      }
+      fence_before_sync();
+      __syncthreads();
+    }
+  }
+  cp_async_wait<0>();
+  // Drain MMAs still tracked (only after an error), with the same time limit.
+  for (int s = 0; s < kStages; ++s)
+    if (pending & (1u << s)) mbar_wait(bars + s, (phases >> s) & 1u, kWaitNs);
+  fence_before_sync();
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    fence_after_sync();
+    tmem_dealloc(tmem, 64);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Chain: recompute a1..a3, then dh3 -> df
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(kThreads, 1) radial_chain_kernel(RadialArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = aligned_smem(smem_raw);
+  constexpr uint32_t kSH = kHiddenImage;             // 147,456
+  constexpr uint32_t kSBar = kSH + 65536;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kSBar);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + kSBar + 8);
+  copy_flat(smem, a.image, kHiddenImage);
+  if (threadIdx.x == 0) mbar_init(bar, 1);
+  if (threadIdx.x < 32) tmem_alloc(slot, 256);
+  fence_async_smem();
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = *slot;
+  const uint32_t lane = (threadIdx.x / 32) * 32;
+  const uint32_t base = smem_u32(smem);
+  const uint32_t r = threadIdx.x;
+  const uint32_t trow = tmem + (lane << 16);
+  uint32_t phase = 0;
+  const int64_t tiles = (a.edges + kTile - 1) / kTile;
+  const uint32_t id64 = idesc_tf32(kTile, kHidden);
+
+  auto issue = [&](auto&& body) {
+    fence_async_smem();
+    fence_before_sync();
+    __syncthreads();
+    if (r == 0) {
+      fence_after_sync();
+      body();
+      mma_commit(bar);
+    }
+  };
+
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int64_t e = t * kTile + r;
+    put_features(smem + kSH, a, e, r);
+    issue([&] { gemm_layer1(tmem, base + kSH, base + kOffW1); });
+    bool ok = wait_all(bar, phase, a.status);
+    // Forward recompute: keep s*silu'(a_l) in TMEM columns 64 + 64*l.
+    for (int layer = 0; ok && layer < 3; ++layer) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float v[16], d[16];
+        tmem_load16(trow + 16 * q, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          d[i] = silu_scaled_grad(v[i]);
+          v[i] = silu_scaled(v[i]);
+        }
+        tmem_store16(trow + 64 + 64 * layer + 16 * q, d);
+        if (layer < 2) put_operand16(smem + kSH, r, 16 * q, v);
+      }
+      if (layer < 2) {
+        issue([&] { gemm_k64(tmem, base + kSH, base + (layer == 0 ? kOffW2 : kOffW3), kHidden, id64); });
+        ok = wait_all(bar, phase, a.status);
+      }
+    }
+    if (!ok) break;
+    // da3 = dh3 * s*silu'(a3)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float v[16], d[16];
+      tmem_load16(trow + 192 + 16 * q, d);
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) {
+        float4 g = e < a.edges ? __ldg(reinterpret_cast<const float4*>(a.grad_h3 + e * kHidden + 16 * q + i))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[i] = g.x * d[i];
+        v[i + 1] = g.y * d[i + 1];
+        v[i + 2] = g.z * d[i + 2];
+        v[i + 3] = g.w * d[i + 3];
+      }
+      put_operand16(smem + kSH, r, 16 * q, v);
+    }
+    // dh2 = da3 W3, da2 = dh2 * s2; dh1 = da2 W2, da1 = dh1 * s1.
+    for (int layer = 1; ok && layer >= 0; --layer) {
+      issue([&] { gemm_k64(tmem, base + kSH, base + (layer == 1 ? kOffW3T : kOffW2T), kHidden, id64); });
+      ok = wait_all(bar, phase, a.status);
+      if (!ok) break;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float v[16], d[16];
+        tmem_load16(trow + 16 * q, v);
+        tmem_load16(trow + 64 + 64 * layer + 16 * q, d);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] *= d[i];
+        put_operand16(smem + kSH, r, 16 * q, v);
+      }
+    }
+    if (!ok) break;
+    // df = da1 W1 (N = 16, columns >= F are zero).
+    issue([&] { gemm_k64(tmem, base + kSH, base + kOffW1T, 16, idesc_tf32(kTile, 16)); });
+    ok = wait_all(bar, phase, a.status);
+    if (!ok) break;
+    {
+      float v[16];
+      tmem_load16(trow, v);
+      if (e < a.edges)
+        for (int i = 0; i < a.features; ++i) a.grad_feats[e * a.features + i] = v[i];
+    }
+    fence_before_sync();
+    __syncthreads();
+  }
+  fence_before_sync();
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    fence_after_sync();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+template <int NC>
+constexpr uint32_t forward_smem() {
+  return kOffW3T + NC * 512 + 65536 + 64 + 1024;
+}
+constexpr uint32_t kAdjointSmem = kStages * kStageBytes + 8 * kStages + 64 + 1024;
+constexpr uint32_t kChainSmem = kHiddenImage + 65536 + 64 + 1024;
+
+int sm_count() {
+  int device = 0, sms = 0;
+  cudaGetDevice(&device);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  return sms > 0 ? sms : 1;
+}
+
+template <class K>
+int prepare_kernel(K kernel, uint32_t smem) {
+  // Per-device attribute: set on every call (cheap) so multi-GPU processes are covered.
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (err != cudaSuccess) {
+    ictc_set_error("radial MLP: %s", cudaGetErrorString(err));
+    return ICTC_ERR_CUDA;
+  }
+  return ICTC_OK;
+}
+
+template <int NC>
+int launch_forward(const RadialArgs& a, cudaStream_t s) {
+  constexpr uint32_t smem = forward_smem<NC>();
+  static_assert(forward_smem<NC>() <= 232448, "forward shared memory");
+  if (int st = prepare_kernel(radial_forward_kernel<NC>, smem)) return st;
+  const int64_t tiles = (a.edges + kTile - 1) / kTile;
+  int per_group = sm_count() / a.groups;
+  if (per_group < 1) per_group = 1;
+  if (per_group > tiles) per_group = (int)tiles;
+  radial_forward_kernel<NC><<<a.groups * per_group, kThreads, smem, s>>>(a);
+  return ICTC_OK;
+}
+
+// Host copy of the 3xTF32 split.
+void split(float x, float* hi, float* lo) {
+  uint32_t bits;
+  std::memcpy(&bits, &x, 4);
+  bits = tf32_round_bits(bits);
+  std::memcpy(hi, &bits, 4);
+  *lo = x - *hi;
+}
+
+void put(unsigned char* img, uint32_t off, float v) { std::memcpy(img + off, &v, 4); }
+
+// K-major hi/lo image of B[n][k] (rows x 64), hi atoms then lo atoms.
+template <class F>
+void pack_square(unsigned char* img, uint32_t rows, F value) {
+  for (uint32_t n = 0; n < rows; ++n)
+    for (uint32_t k = 0; k < (uint32_t)kHidden; ++k) {
+      float hi, lo;
+      split(value(n, k), &hi, &lo);
+      put(img, sw128_offset(rows, n, k), hi);
+      put(img, 2 * rows * kAtomBytes + sw128_offset(rows, n, k), lo);
+    }
+}
+
+}  // namespace
+}  // namespace ictc
+
+using namespace ictc;
+
+extern "C" int64_t ictc_radial_image_bytes(int features, int hidden, int gates) {
+  RadialShape s;
+  if (!radial_shape(features, hidden, gates, &s)) return -1;
+  return (int64_t)s.total;
+}
+
+extern "C" int ictc_radial_pack(const float* w1, const float* w2, const float* w3, const float* w4, int features,
+                                int hidden, int gates, void* image, int64_t image_bytes) {
+  RadialShape s;
+  if (!radial_shape(features, hidden, gates, &s)) {
+    ictc_set_error("ictc_radial_pack: unsupported shape (F <= 8, hidden 64, gates a multiple of 32)%s", "");
+    return ICTC_ERR_UNSUPPORTED;
+  }
+  if (!w1 || !w2 || !w3 || !w4 || !image || image_bytes < (int64_t)s.total) {
+    ictc_set_error("ictc_radial_pack: invalid argument%s", "");
+    return ICTC_ERR_INVALID;
+  }
+  unsigned char* img = static_cast<unsigned char*>(image);
+  std::memset(img, 0, s.total);
+  const int F = features, H = kHidden;
+  // W1 [64, F]: hi at k 0-7, lo at k 8-15 of each row.
+  for (int n = 0; n < H; ++n)
+    for (int k = 0; k < F; ++k) {
+      float hi, lo;
+      split(w1[n * F + k], &hi, &lo);
+      put(img + kOffW1, sw128_offset(H, n, k), hi);
+      put(img + kOffW1, sw128_offset(H, n, 8 + k), lo);
+    }
+  pack_square(img + kOffW2, H, [&](uint32_t n, uint32_t k) { return w2[n * H + k]; });
+  pack_square(img + kOffW3, H, [&](uint32_t n, uint32_t k) { return w3[n * H + k]; });
+  pack_square(img + kOffW3T, H, [&](uint32_t n, uint32_t k) { return w3[k * H + n]; });
+  pack_square(img + kOffW2T, H, [&](uint32_t n, uint32_t k) { return w2[k * H + n]; });
+  pack_square(img + kOffW1T, 16, [&](uint32_t n, uint32_t k) { return (int)n < F ? w1[k * F + n] : 0.f; });
+  // W4 [G, 64] in forward column groups of nc rows.
+  for (int g = 0; g < s.groups; ++g)
+    pack_square(img + s.w4 + (uint64_t)g * s.nc * 512, s.nc,
+                [&](uint32_t n, uint32_t k) { return w4[(uint64_t)(g * s.nc + n) * H + k]; });
+  // W4^T chunks for the adjoint: chunk c = rows n (64) x k in [32c, 32c+32).
+  for (int c = 0; c < s.chunks; ++c) {
+    unsigned char* chunk = img + s.w4t + (uint64_t)c * 16384;
+    for (int n = 0; n < H; ++n)
+      for (int k = 0; k < 32; ++k) {
+        float hi, lo;
+        split(w4[(uint64_t)(32 * c + k) * H + n], &hi, &lo);
+        put(chunk, sw128_offset(H, n, k), hi);
+        put(chunk + 8192, sw128_offset(H, n, k), lo);
+      }
+  }
+  return ICTC_OK;
+}
+
+extern "C" int ictc_radial_forward(const void* image, const float* feats, float* gates, int64_t edges,
+                                   int features, int hidden, int gates_width, int* status, void* stream) {
+  RadialShape s;
+  if (!radial_shape(features, hidden, gates_width, &s)) {
+    ictc_set_error("ictc_radial_forward: unsupported shape%s", "");
+    return ICTC_ERR_UNSUPPORTED;
+  }
+  if (edges < 0 || (edges > 0 && (!image || !feats || !gates))) {
+    ictc_set_error("ictc_radial_forward: invalid argument%s", "");
+    return ICTC_ERR_INVALID;
+  }
+  if (edges == 0) return ICTC_OK;
+  RadialArgs a{};
+  a.image = static_cast<const unsigned char*>(image);
+  a.feats = feats;
+  a.gates = gates;
+  a.status = status;
+  a.edges = edges;
+  a.features = features;
+  a.gates_width = gates_width;
+  a.nc = s.nc;
+  a.groups = s.groups;
+  a.chunks = s.chunks;
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc;
+  switch (s.nc) {
+    case 176: rc = launch_forward<176>(a, st); break;
+    case 160: rc = launch_forward<160>(a, st); break;
+    case 128: rc = launch_forward<128>(a, st); break;
+    case 96: rc = launch_forward<96>(a, st); break;
+    case 64: rc = launch_forward<64>(a, st); break;
+    default: rc = launch_forward<32>(a, st); break;
+  }
+  if (rc) return rc;
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) {
+    ictc_set_error("ictc_radial_forward: %s", cudaGetErrorString(err));
+    return ICTC_ERR_CUDA;
+  }
+  return ICTC_OK;
+}
+
+extern "C" int ictc_radial_backward(const void* image, const float* feats, const float* grad_gates,
+                                    float* grad_h3, float* grad_feats, int64_t edges, int features, int hidden,
+                                    int gates_width, int* status, void* stream) {
+  RadialShape s;
+  if (!radial_shape(features, hidden, gates_width, &s)) {
+    ictc_set_error("ictc_radial_backward: unsupported shape%s", "");
+    return ICTC_ERR_UNSUPPORTED;
+  }
+  if (edges < 0 || (edges > 0 && (!image || !feats || !grad_gates || !grad_h3 || !grad_feats))) {
+    ictc_set_error("ictc_radial_backward: invalid argument%s", "");
+    return ICTC_ERR_INVALID;
+  }
+  if (edges == 0) return ICTC_OK;
+  RadialArgs a{};
+  a.image = static_cast<const unsigned char*>(image);
+  a.feats = feats;
+  a.grad_gates = grad_gates;
+  a.grad_h3 = grad_h3;
+  a.out_h3 = grad_h3;
+  a.grad_feats = grad_feats;
+  a.status = status;
+  a.edges = edges;
+  a.features = features;
+  a.gates_width = gates_width;
+  a.nc = s.nc;
+  a.groups = s.groups;
+  a.chunks = s.chunks;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (int rc = prepare_kernel(radial_w4_adjoint_kernel, kAdjointSmem)) return rc;
+  if (int rc = prepare_kernel(radial_chain_kernel, kChainSmem)) return rc;
+  const int64_t tiles = (edges + kTile - 1) / kTile;
+  const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
+  radial_w4_adjoint_kernel<<<grid, kThreads, kAdjointSmem, st>>>(a);
+  radial_chain_kernel<<<grid, kThreads, kChainSmem, st>>>(a);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) {
+    ictc_set_error("ictc_radial_backward: %s", cudaGetErrorString(err));
+    return ICTC_ERR_CUDA;
+  }
+  return ICTC_OK;
+}

@@ -42,9 +42,14 @@ _SIGNATURES = {
     "ictc_neighbor_noalloc_scratch_bytes": [],
     "ictc_neighbor_list_noalloc": [_p, _i64, _p, ctypes.c_float, _p, _p, _p, _p, _i64, _p],
     "ictc_direction_harmonics": [_p, _p, _p, _p, _p, _p, _i64, _i, _i, _p],
+    "ictc_radial_image_bytes": [_i, _i, _i],
+    "ictc_radial_pack": [_p, _p, _p, _p, _i, _i, _i, _p, _i64],
+    "ictc_radial_forward": [_p, _p, _p, _i64, _i, _i, _i, _p, _p],
+    "ictc_radial_backward": [_p, _p, _p, _p, _p, _i64, _i, _i, _i, _p, _p],
 }
 _RESTYPES = {"ictc_last_error": ctypes.c_char_p, "ictc_sc_table_rows": _i64,
-             "ictc_neighbor_workspace_bytes": _i64, "ictc_neighbor_noalloc_scratch_bytes": _i64}
+             "ictc_neighbor_workspace_bytes": _i64, "ictc_neighbor_noalloc_scratch_bytes": _i64,
+             "ictc_radial_image_bytes": _i64}
 
 _lock = threading.Lock()
 _lib = None

@@ -50,6 +50,19 @@ class CudaOps:
     def contraction(self, module, features, species):
         return module(features, node_type_idx=species)
 
+    def radial(self, fc, feats):
+        """Gates of the radial MLP: fused tensor-core kernels when the shape is supported."""
+        from ictc_o3.backends.cuda import radial
+        linears = [m for m in fc if isinstance(m, nn.Linear)]
+        shape = (linears[0].in_features, linears[0].out_features, linears[-1].out_features)
+        plan = fc.__dict__.get("_ictc_radial_plan")
+        if plan is None:
+            plan = radial.RadialPlan() if radial.supported(*shape) else False
+            fc.__dict__["_ictc_radial_plan"] = plan
+        if plan is False:
+            return fc(feats)
+        return radial.radial_gates(linears, feats, plan)
+
 
 # ---------------------------------------------------------------------------
 # Radial embedding (mace_ictc/models/radial_basis.py:11-92)
@@ -194,7 +207,8 @@ class InteractionBlock(nn.Module):
         """Messages into the first ``owned`` nodes (all nodes by default); ``groups`` index those."""
         owned = node_feats.shape[0] if owned is None else owned
         x_up = self.linear_up(node_feats)
-        gates = self.fc(edge_feats)
+        radial = getattr(ops, "radial", None)
+        gates = radial(self.fc, edge_feats) if radial is not None else self.fc(edge_feats)
         msg = ops.message(self.tp, x_up, edge_harmonics, gates, src, dst, mask, owned)
         message = self.message_linear(msg) / max(self.avg_num_neighbors, 1e-8)
         if self.self_connection is None:

@@ -211,6 +211,31 @@ int ictc_neighbor_fill_receivers(const float* pos, int64_t atoms, int64_t receiv
                                  const int64_t* offsets, int64_t* src, int64_t* dst, float* shift, void* stream);
 
 /*
+ * Fused radial MLP of the MACE interaction (tcgen05 tensor cores, 3xTF32):
+ *   gates = W4 s*silu(W3 s*silu(W2 s*silu(W1 f)))     (bias-free, s = 1.6791767923989418)
+ * for edge embeddings f [E, F] (F <= 8), hidden width 64 and G gate columns
+ * (a multiple of 32).  Replaces the radial network `fc` evaluated per edge in
+ * mace_ictc/models/pure_cartesian_ictd_fix.py:1545-1553 (the gates of
+ * radial_graph_message, ictc_o3/backends/ascend/capacity_message.py:109-179).
+ *   ictc_radial_image_bytes: size of the packed weight image (-1 if unsupported).
+ *   ictc_radial_pack: HOST function; packs w1 [64, F], w2 [64, 64], w3 [64, 64],
+ *     w4 [G, 64] (row-major, nn.Linear [out, in]) into `image` (host memory) as
+ *     TF32 hi/lo pairs in the kernels' shared-memory layout; copy it to the device.
+ *   ictc_radial_forward: gates [E, G] from f [E, F].
+ *   ictc_radial_backward: grad_f [E, F] from grad_gates [E, G]; grad_h3 [E, 64]
+ *     is device scratch (dL/dh3).
+ *   status: optional device int, set non-zero if a wait inside the kernel timed out.
+ */
+int64_t ictc_radial_image_bytes(int features, int hidden, int gates);
+int ictc_radial_pack(const float* w1, const float* w2, const float* w3, const float* w4, int features, int hidden,
+                     int gates, void* image, int64_t image_bytes);
+int ictc_radial_forward(const void* image, const float* feats, float* gates, int64_t edges, int features,
+                        int hidden, int gates_width, int* status, void* stream);
+int ictc_radial_backward(const void* image, const float* feats, const float* grad_gates, float* grad_h3,
+                         float* grad_feats, int64_t edges, int features, int hidden, int gates_width, int* status,
+                         void* stream);
+
+/*
  * Allocation-free neighbour search.  No counterpart in the reference: it exists
  * for callers that cannot allocate device memory during a step (an MD engine
  * that owns all device buffers in its own pool, or a host program using this C

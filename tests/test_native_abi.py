@@ -53,3 +53,73 @@ def test_operators_reject_host_tensors():
         EdgeTensorProduct.create(channels=64, input_lmax=2, edge_lmax=2, device="cpu")
     with pytest.raises(ValueError):
         direction_harmonics(torch.zeros(4, 3), 2)
+
+
+def _sw128(rows, r, k):
+    """Byte offset of fp32 element (r, k) in a K-major tile with the 128-byte swizzle."""
+    atom, kk = divmod(k, 32)
+    return atom * rows * 128 + r * 128 + (((kk // 4) ^ (r % 8)) * 16) + (kk % 4) * 4
+
+
+def test_radial_weight_image_round_trips():
+    """ictc_radial_pack (host): every weight equals hi + lo at its swizzled position,
+    hi is a TF32 value, and the transposed copies hold the transposes."""
+    import numpy as np
+    import torch
+    from ictc_o3.backends.cuda import radial
+    torch.manual_seed(0)
+    F, H, G = 6, 64, 192
+    ws = [torch.randn(H, F), torch.randn(H, H), torch.randn(H, H), torch.randn(G, H)]
+    img = radial.pack_image(ws).numpy()
+    assert img.size == _native_size(F, H, G)
+
+    def read(off):
+        return np.frombuffer(img[off:off + 4].tobytes(), dtype=np.float32)[0]
+
+    def check(base, rows, value, n, k):
+        hi = read(base + _sw128(rows, n, k))
+        lo = read(base + 2 * rows * 128 + _sw128(rows, n, k))
+        assert np.frombuffer(np.float32(hi).tobytes(), np.uint32)[0] & 0x1FFF == 0
+        assert abs((np.float64(hi) + np.float64(lo)) - float(value)) <= 1e-7 * max(1.0, abs(float(value)))
+
+    w1, w2, w3, w4 = (w.numpy() for w in ws)
+    for n in range(0, H, 7):
+        for k in range(F):
+            hi, lo = read(_sw128(H, n, k)), read(_sw128(H, n, 8 + k))
+            assert abs(float(hi) + float(lo) - float(w1[n, k])) <= 1e-7 * max(1.0, abs(float(w1[n, k])))
+        for k in range(0, H, 5):
+            check(8192, H, w2[n, k], n, k)
+            check(8192 + 32768, H, w3[n, k], n, k)
+            check(8192 + 2 * 32768, H, w3[k, n], n, k)
+            check(8192 + 3 * 32768, H, w2[k, n], n, k)
+    for n in range(F):
+        for k in range(0, H, 3):
+            check(8192 + 4 * 32768, 16, w1[k, n], n, k)
+    w4_base = 8192 + 4 * 32768 + 8192
+    nc = 96                                     # largest supported group width dividing 192
+    for g in range(G // nc):
+        for n in range(0, nc, 11):
+            for k in range(0, H, 9):
+                check(w4_base + g * nc * 512, nc, w4[g * nc + n, k], n, k)
+    w4t_base = w4_base + G * 512
+    for c in range(G // 32):
+        for n in range(0, H, 13):
+            for k in range(0, 32, 7):
+                hi = read(w4t_base + c * 16384 + _sw128(H, n, k))
+                lo = read(w4t_base + c * 16384 + 8192 + _sw128(H, n, k))
+                want = float(w4[32 * c + k, n])
+                assert abs(float(hi) + float(lo) - want) <= 1e-7 * max(1.0, abs(want))
+
+
+def _native_size(F, H, G):
+    from ictc_o3.backends.cuda import _native
+    return int(_native.library().ictc_radial_image_bytes(F, H, G))
+
+
+def test_radial_rejects_unsupported_shapes():
+    from ictc_o3.backends.cuda import _native
+    lib = _native.library()
+    assert lib.ictc_radial_image_bytes(9, 64, 192) == -1
+    assert lib.ictc_radial_image_bytes(8, 32, 192) == -1
+    assert lib.ictc_radial_image_bytes(8, 64, 100) == -1
+    assert lib.ictc_radial_forward(None, None, None, 10, 8, 64, 192, None, None) == -1
