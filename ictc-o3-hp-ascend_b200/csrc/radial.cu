@@ -6,11 +6,9 @@
 //     h1 = s*silu(f W1^T), h2 = s*silu(h1 W2^T), h3 = s*silu(h2 W3^T), gates = h3 W4^T
 // with bias-free linears (F -> 64 -> 64 -> 64 -> G) and the normalised SiLU scale s.
 //
-// radial_forward_kernel: one CTA per SM, a tile of 128 edges at a time; the three
-//   hidden layers stay on chip (TMEM accumulators, shared-memory operands) and only
-//   the gates are written.  W4's rows are split into column groups so that one group
-//   plus the hidden weights fit in shared memory; each group recomputes the (cheap)
-//   hidden layers.
+// radial_forward_kernel: one CTA per SM, tiles of 128 edges; warp-specialised (a
+//   control thread issuing MMAs and bulk copies, a hidden-layer warp group and an
+//   output warp group); the hidden activations stay on chip and W4 streams from L2.
 // radial_w4_adjoint_kernel: dh3 = dgates W4, a streaming GEMM over K = G with a
 //   4-stage cp.async pipeline (dgates from HBM, W4^T chunks from L2).
 // radial_chain_kernel: recomputes the hidden layers, keeps s*silu'(a_l) in TMEM and
@@ -37,7 +35,19 @@ using namespace tc;
 constexpr int kHidden = 64;
 constexpr int kMaxFeatures = 8;
 constexpr int kTile = 128;             // edges per tile = MMA M
-constexpr int kThreads = 128;          // thread r owns tile row r (TMEM lane r)
+constexpr int kThreads = 512;          // 4 warpgroups; see Slot
+
+// Thread layout: warp w reads TMEM lanes 32*(w % 4) .. +31 (tile rows) and owns the
+// column slice w / 4 of every epilogue, so four warps share each row's work.
+struct Slot {
+  uint32_t row, slice, lane_base;
+  __device__ Slot() {
+    const uint32_t warp = threadIdx.x / 32;
+    row = (warp % 4) * 32 + threadIdx.x % 32;
+    slice = warp / 4;
+    lane_base = ((warp % 4) * 32) << 16;
+  }
+};
 constexpr float kSiluScale = 1.6791767923989418f;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s: far above any legitimate wait
 
@@ -50,21 +60,14 @@ constexpr uint32_t kOffW1 = 0, kOffW2 = kOffW1 + kW1, kOffW3 = kOffW2 + kSquare,
 constexpr uint32_t kHiddenImage = kOffW4;                         // 147,456: W1..W1T
 
 struct RadialShape {
-  int features, gates, nc, groups, chunks;
+  int features, gates, chunks;
   uint64_t w4, w4t, total;
 };
 
 bool radial_shape(int features, int hidden, int gates, RadialShape* s) {
-  if (features < 1 || features > kMaxFeatures || hidden != kHidden || gates < 32 || gates % 32) return false;
+  if (features < 1 || features > kMaxFeatures || hidden != kHidden || gates < 64 || gates % 64) return false;
   s->features = features;
   s->gates = gates;
-  s->nc = 0;
-  for (int nc : {176, 160, 128, 96, 64, 32})
-    if (gates % nc == 0) {
-      s->nc = nc;
-      break;
-    }
-  s->groups = gates / s->nc;
   s->chunks = gates / 32;
   s->w4 = kOffW4;
   s->w4t = s->w4 + (uint64_t)gates * 512u;
@@ -82,16 +85,18 @@ struct RadialArgs {
   float* grad_feats;         // [E, F]
   int* status;
   int64_t edges;
-  int features, gates_width, nc, groups, chunks;
+  int features, gates_width, chunks;
 };
 
 __device__ __forceinline__ void flag_error(int* status, int code) {
   if (status) atomicExch(status, code);
 }
 
-__device__ __forceinline__ float silu_scaled(float a) { return kSiluScale * a / (1.0f + __expf(-a)); }
+// Logistic function; the exponent is clamped so 1 + e stays finite.
+__device__ __forceinline__ float sigmoid(float a) { return __frcp_rn(1.0f + __expf(fminf(-a, 80.0f))); }
+__device__ __forceinline__ float silu_scaled(float a) { return kSiluScale * a * sigmoid(a); }
 __device__ __forceinline__ float silu_scaled_grad(float a) {
-  const float sig = 1.0f / (1.0f + __expf(-a));
+  const float sig = sigmoid(a);
   return kSiluScale * sig * (1.0f + a * (1.0f - sig));
 }
 
@@ -169,93 +174,250 @@ __device__ __forceinline__ unsigned char* aligned_smem(unsigned char* raw) {
 }
 
 // ---------------------------------------------------------------------------
-// Forward
+// Forward (warp-specialised, activations in TMEM)
+//
+//   warp 0, lane 0  control: issues every MMA and the bulk copies of W4 chunks;
+//   warps 4..11     hidden group: features and s*silu epilogues, written to TMEM;
+//   warps 12..19    output group: gate chunks TMEM -> HBM.
+// TMEM columns: [0,64) hidden accumulator, [64,128) / [128,192) hidden activation
+// hi / lo (the A operand of the next layer), [192,200) / [200,208) features hi / lo,
+// [256,512) four 64-column gate slots.  A operands are read from TMEM, so an MMA
+// only reads its weights from shared memory.
+// Per tile: L1, L2, L3, then G/64 chunk MMAs (h3 x W4 rows of the chunk, N = 64) into
+// the slot ring that the output group drains while the next tile's hidden layers
+// run; the output group stages each chunk in shared memory and writes whole row
+// segments (coalesced).  W4 chunks (32 KB, hi + lo) stream from L2 through a
+// 3-stage shared ring; a stage is refilled once the MMAs that read it two chunks
+// earlier are done.
 // ---------------------------------------------------------------------------
 
-template <int NC>
-__global__ void __launch_bounds__(kThreads, 1) radial_forward_kernel(RadialArgs a) {
+constexpr int kFwdThreads = 640;
+constexpr int kW4Stages = 3, kW4Lag = 2, kD4Slots = 4, kW4Rows = 64;
+constexpr uint32_t kW4Chunk = 2 * 2 * kW4Rows * kAtomBytes;  // 32 KB: 64 rows x 64 K, hi + lo
+constexpr uint32_t kFwdW4 = kOffW3T;                         // W4 ring after W1, W2, W3
+constexpr uint32_t kStageRow = kW4Rows * 4 + 16;             // padded row of the output staging
+constexpr uint32_t kFwdOut = kFwdW4 + kW4Stages * kW4Chunk;  // gate chunk staging [128][kStageRow]
+constexpr uint32_t kFwdBar = kFwdOut + kTile * kStageRow;
+constexpr uint32_t kFwdSmem = kFwdBar + 256 + 1024;
+constexpr uint32_t kColH = 64, kColHLo = 128, kColF = 192, kColFLo = 200, kColOut = 256;
+
+struct FwdBars {
+  uint64_t op_ready, acc_full, h_free;
+  uint64_t w4_full[kW4Stages], w4_empty[kW4Stages];
+  uint64_t d4_full[kD4Slots], d4_empty[kD4Slots];
+  uint32_t tmem_slot;
+  int abort;
+};
+
+// D = A[TMEM, 128 x 64 hi/lo] * B[smem image, rows x 64]^T.
+__device__ __forceinline__ void gemm_k64_ta(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint32_t b, uint32_t rows,
+                                            uint32_t idesc) {
+#pragma unroll
+  for (uint32_t kk = 0; kk < 8; ++kk) {
+    const uint32_t bo = (kk / 4) * rows * kAtomBytes + (kk % 4) * 32;
+    mma_tf32x3_ta(d, a_hi + 8 * kk, a_lo + 8 * kk, b + bo, b + 2 * rows * kAtomBytes + bo, idesc,
+                  kk > 0 ? 1u : 0u);
+  }
+}
+
+__global__ void __launch_bounds__(kFwdThreads, 1) radial_forward_kernel(RadialArgs a) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = aligned_smem(smem_raw);
-  constexpr uint32_t kSW4 = kOffW3T;                 // W1, W2, W3 occupy [0, kOffW3T)
-  constexpr uint32_t kSH = kSW4 + NC * 512;          // hidden operand, 64 KB
-  constexpr uint32_t kSBar = kSH + 65536;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kSBar);
-  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + kSBar + 8);
+  FwdBars* b = reinterpret_cast<FwdBars*>(smem + kFwdBar);
+  volatile int* abort = &b->abort;
+  const uint32_t warp = threadIdx.x / 32;
+  const int chunks = a.gates_width / kW4Rows;
+  const int64_t tiles = (a.edges + kTile - 1) / kTile;
 
-  const int group = blockIdx.x % a.groups;
-  const int first = blockIdx.x / a.groups, stride = gridDim.x / a.groups;
-  copy_flat(smem, a.image, kOffW3T);
-  copy_flat(smem + kSW4, a.image + kOffW4 + (uint64_t)group * NC * 512, NC * 512);
-  if (threadIdx.x == 0) mbar_init(bar, 1);
-  if (threadIdx.x < 32) tmem_alloc(slot, 256);
+  copy_flat(smem, a.image, kOffW3T);                 // W1, W2, W3
+  if (threadIdx.x == 0) {
+    mbar_init(&b->op_ready, 1);
+    mbar_init(&b->acc_full, 1);
+    mbar_init(&b->h_free, 1);
+    for (int i = 0; i < kW4Stages; ++i) {
+      mbar_init(&b->w4_full[i], 1);
+      mbar_init(&b->w4_empty[i], 1);
+    }
+    for (int i = 0; i < kD4Slots; ++i) {
+      mbar_init(&b->d4_full[i], 1);
+      mbar_init(&b->d4_empty[i], 8);
+    }
+    b->abort = 0;
+  }
+  if (warp == 0) tmem_alloc(&b->tmem_slot, 512);
   fence_async_smem();
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
-  const uint32_t tmem = *slot;
-  const uint32_t lane = (threadIdx.x / 32) * 32;
+  const uint32_t tmem = b->tmem_slot;
   const uint32_t base = smem_u32(smem);
-  const uint32_t r = threadIdx.x;
-  uint32_t phase = 0;
-  const int64_t tiles = (a.edges + kTile - 1) / kTile;
+  const unsigned char* w4_image = a.image + kOffW4;
+  const uint32_t id64 = idesc_tf32(kTile, kHidden);
 
-  for (int64_t t = first; t < tiles; t += stride) {
-    const int64_t e = t * kTile + r;
-    put_features(smem + kSH, a, e, r);
-    fence_async_smem();
-    __syncthreads();
-    if (r == 0) {
-      fence_after_sync();
-      gemm_layer1(tmem, base + kSH, base + kOffW1);
-      mma_commit(bar);
-    }
-    bool ok = wait_all(bar, phase, a.status);
-    for (int layer = 0; ok && layer < 3; ++layer) {
-      // Epilogue: h = s * silu(D) into the operand buffer.
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float v[16];
-        tmem_load16(tmem + (lane << 16) + 16 * q, v);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = silu_scaled(v[i]);
-        put_operand16(smem + kSH, r, 16 * q, v);
-      }
-      fence_async_smem();
-      fence_before_sync();
-      __syncthreads();
-      if (r == 0) {
+  if (warp == 0) {
+    if (threadIdx.x == 0) {
+      // ----- control -----
+      uint32_t op_phase = 0, full_phase[kW4Stages] = {}, empty_phase[kW4Stages] = {}, d4e_phase[kD4Slots] = {};
+      int64_t wcount = 0, issued = 0;                // W4 chunks consumed / requested (CTA lifetime)
+      const int64_t my_tiles = tiles > blockIdx.x ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+      const int64_t total_chunks = my_tiles * chunks;
+      auto request = [&](int64_t n) {                // bulk-load chunk sequence item n into its stage
+        const int st = (int)(n % kW4Stages);
+        mbar_arrive_expect(&b->w4_full[st], kW4Chunk);
+        bulk_load(smem + kFwdW4 + st * kW4Chunk, w4_image + (uint64_t)(n % chunks) * kW4Chunk, kW4Chunk,
+                  &b->w4_full[st]);
+      };
+      for (; issued < total_chunks && issued < kW4Stages - kW4Lag; ++issued) request(issued);
+      bool ok = true;
+      auto wait_op = [&]() {
+        ok = ok && mbar_wait_or_abort(&b->op_ready, op_phase, kWaitNs, abort);
+        op_phase ^= 1u;
         fence_after_sync();
-        if (layer < 2) {
-          gemm_k64(tmem, base + kSH, base + (layer == 0 ? kOffW2 : kOffW3), kHidden, idesc_tf32(kTile, kHidden));
-        } else {
-          gemm_k64(tmem + 64, base + kSH, base + kSW4, NC, idesc_tf32(kTile, NC));
+        return ok;
+      };
+      for (int64_t i = 0; i < my_tiles && ok; ++i) {
+        if (!wait_op()) break;                       // features in TMEM
+        mma_tf32x3_ta(tmem, tmem + kColF, tmem + kColFLo, base + kOffW1, base + kOffW1 + 32, id64, 0u);
+        mma_commit(&b->acc_full);
+        for (int layer = 0; layer < 2 && ok; ++layer) {
+          if (!wait_op()) break;                     // h1, h2 in TMEM
+          gemm_k64_ta(tmem, tmem + kColH, tmem + kColHLo, base + (layer == 0 ? kOffW2 : kOffW3), kHidden, id64);
+          mma_commit(&b->acc_full);
         }
-        mma_commit(bar);
+        if (!ok || !wait_op()) break;                // h3 in TMEM
+        for (int j = 0; j < chunks && ok; ++j, ++wcount) {
+          const int st = (int)(wcount % kW4Stages), slot = (int)(wcount % kD4Slots);
+          if (issued < total_chunks) {               // refill the stage read kW4Lag chunks ago
+            const int fs = (int)(issued % kW4Stages);
+            if (issued >= kW4Stages) {
+              ok = mbar_wait_or_abort(&b->w4_empty[fs], empty_phase[fs], kWaitNs, abort);
+              empty_phase[fs] ^= 1u;
+              if (!ok) break;
+            }
+            request(issued++);
+          }
+          ok = mbar_wait_or_abort(&b->w4_full[st], full_phase[st], kWaitNs, abort);
+          full_phase[st] ^= 1u;
+          if (ok && wcount >= kD4Slots) {
+            ok = mbar_wait_or_abort(&b->d4_empty[slot], d4e_phase[slot], kWaitNs, abort);
+            d4e_phase[slot] ^= 1u;
+          }
+          if (!ok) break;
+          fence_after_sync();
+          gemm_k64_ta(tmem + kColOut + kW4Rows * slot, tmem + kColH, tmem + kColHLo, base + kFwdW4 + st * kW4Chunk,
+                      kW4Rows, idesc_tf32(kTile, kW4Rows));
+          mma_commit(&b->d4_full[slot]);
+          mma_commit(&b->w4_empty[st]);
+        }
+        mma_commit(&b->h_free);                      // h3 may be overwritten once these MMAs finish
       }
-      ok = wait_all(bar, phase, a.status);
     }
-    if (!ok) break;
-    // Gates of this column group: row r, columns [group*NC, group*NC + NC).
-#pragma unroll 1
-    for (int q = 0; q < NC / 16; ++q) {
-      float v[16];
-      tmem_load16(tmem + (lane << 16) + 64 + 16 * q, v);
-      if (e < a.edges) {
-        float4* dst = reinterpret_cast<float4*>(a.gates + e * a.gates_width + group * NC + 16 * q);
-        dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-        dst[1] = make_float4(v[4], v[5], v[6], v[7]);
-        dst[2] = make_float4(v[8], v[9], v[10], v[11]);
-        dst[3] = make_float4(v[12], v[13], v[14], v[15]);
+  } else if (warp >= 4 && warp < 12) {
+    // ----- hidden group: 8 warps, quadrant warp % 4, column half (warp - 4) / 4 -----
+    const uint32_t row = (warp % 4) * 32 + threadIdx.x % 32;
+    const uint32_t half = (warp - 4) / 4;
+    const uint32_t lanes = tmem + (((warp % 4) * 32) << 16);
+    uint32_t acc_phase = 0, hfree_phase = 0;
+    bool ok = true;
+    int64_t count = 0;
+    for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++count) {
+      const int64_t e = t * kTile + row;
+      if (half == 0) {
+        float f[8], hi[8], lo[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          f[i] = (e < a.edges && i < a.features) ? __ldg(a.feats + e * a.features + i) : 0.f;
+          hi[i] = tf32_hi(f[i]);
+          lo[i] = f[i] - hi[i];
+        }
+        tmem_store8(lanes + kColF, hi);
+        tmem_store8(lanes + kColFLo, lo);
+      }
+      fence_before_sync();
+      named_barrier(1, 256);
+      if (threadIdx.x == 128) mbar_arrive(&b->op_ready);
+      for (int layer = 0; layer < 3 && ok; ++layer) {
+        ok = named_barrier_all(1, 256, mbar_wait_or_abort(&b->acc_full, acc_phase, kWaitNs, abort));
+        acc_phase ^= 1u;
+        if (!ok) break;
+        if (layer == 0 && count > 0) {               // the previous tile's W4 MMAs still read h3
+          ok = named_barrier_all(1, 256, mbar_wait_or_abort(&b->h_free, hfree_phase, kWaitNs, abort));
+          hfree_phase ^= 1u;
+          if (!ok) break;
+        }
+        fence_after_sync();
+        float v[32], hi[16], lo[16];
+        tmem_load16(lanes + 32 * half, v);
+        tmem_load16(lanes + 32 * half + 16, v + 16);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float h = silu_scaled(v[16 * q + i]);
+            hi[i] = tf32_hi(h);
+            lo[i] = h - hi[i];
+          }
+          tmem_store16_async(lanes + kColH + 32 * half + 16 * q, hi);
+          tmem_store16_async(lanes + kColHLo + 32 * half + 16 * q, lo);
+        }
+        tmem_store_wait();
+        fence_before_sync();
+        named_barrier(1, 256);
+        if (threadIdx.x == 128) mbar_arrive(&b->op_ready);
       }
     }
-    fence_before_sync();
-    __syncthreads();
+  } else if (warp >= 12) {
+    // ----- output group: 8 warps, quadrant warp % 4, 32-column half of each chunk -----
+    const uint32_t row = (warp % 4) * 32 + threadIdx.x % 32;
+    const uint32_t half = (warp - 12) / 4;
+    const uint32_t lanes = tmem + (((warp % 4) * 32) << 16);
+    uint32_t full_phase[kD4Slots] = {};
+    int64_t wcount = 0;
+    bool ok = true;
+    for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      const int64_t e = t * kTile + row;
+      for (int j = 0; j < chunks; ++j, ++wcount) {
+        const int slot = (int)(wcount % kD4Slots);
+        // Group-wide: all reads of the previous chunk's staging are done, and all agree on ok.
+        ok = named_barrier_all(2, 256, mbar_wait_or_abort(&b->d4_full[slot], full_phase[slot], kWaitNs, abort));
+        full_phase[slot] ^= 1u;
+        if (!ok) break;
+        fence_after_sync();
+        float v[32];
+        tmem_load16(lanes + kColOut + kW4Rows * slot + 32 * half, v);
+        tmem_load16(lanes + kColOut + kW4Rows * slot + 32 * half + 16, v + 16);
+        fence_before_sync();
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(&b->d4_empty[slot]);
+        float4* stage_row = reinterpret_cast<float4*>(smem + kFwdOut + row * kStageRow + 128 * half);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) stage_row[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        named_barrier(2, 256);
+        // 128 rows x 16 float4: 16 consecutive threads write one row's 256 contiguous bytes.
+        const uint32_t ot = threadIdx.x - 384;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint32_t idx = ot + 256 * q, r = idx / 16, c4 = idx % 16;
+          const int64_t er = t * kTile + r;
+          const float4 val = *reinterpret_cast<const float4*>(smem + kFwdOut + r * kStageRow + 16 * c4);
+          if (er < a.edges)
+            *reinterpret_cast<float4*>(a.gates + er * a.gates_width + kW4Rows * j + 4 * c4) = val;
+        }
+      }
+    }
   }
-  fence_before_sync();
+  // Teardown: the control thread's last commit (h_free) covers every MMA it issued.
   __syncthreads();
-  if (threadIdx.x < 32) {
+  if (threadIdx.x == 0 && *abort) flag_error(a.status, 4);
+  if (warp == 0) {
+    const int64_t my_tiles = tiles > blockIdx.x ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    if (my_tiles > 0 && threadIdx.x == 0) {
+      // h_free completes once per tile; the last completion has parity (my_tiles - 1) & 1.
+      mbar_wait(&b->h_free, (uint32_t)((my_tiles - 1) & 1), kWaitNs);
+    }
+    __syncwarp();
     fence_after_sync();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -265,6 +427,10 @@ __global__ void __launch_bounds__(kThreads, 1) radial_forward_kernel(RadialArgs 
 
 constexpr int kStages = 4;
 constexpr uint32_t kStageBytes = 3 * 16384;  // A hi, A lo, B (W4^T chunk hi+lo)
+// K chunks rotate over independent TMEM accumulators, summed in FP32 at the end:
+// the tensor core's accumulation error grows with the K it sums, and G reaches
+// thousands.
+constexpr int kAccumulators = 8;
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
@@ -276,7 +442,7 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 __device__ __forceinline__ void issue_chunk(const RadialArgs& a, uint32_t stage, int64_t tile, int chunk) {
   // A: rows of dgates, 32 values (8 x 16 B) per row, swizzled into the A-hi buffer.
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < 1024 / kThreads; ++i) {
     const uint32_t idx = threadIdx.x + kThreads * i;
     const uint32_t r = idx / 8, ch = idx % 8;
     const int64_t e = tile * kTile + r;
@@ -287,7 +453,7 @@ __device__ __forceinline__ void issue_chunk(const RadialArgs& a, uint32_t stage,
   // B: the chunk's W4^T image (hi 8 KB, lo 8 KB), flat.
   const unsigned char* img = a.image + kOffW4 + (uint64_t)a.gates_width * 512u + (uint64_t)chunk * 16384u;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < 1024 / kThreads; ++i) {
     const uint32_t idx = threadIdx.x + kThreads * i;
     cp_async16(stage + 2 * 16384 + idx * 16, img + idx * 16, 16u);
   }
@@ -301,14 +467,15 @@ __global__ void __launch_bounds__(kThreads, 1) radial_w4_adjoint_kernel(RadialAr
   uint32_t* slot = reinterpret_cast<uint32_t*>(smem + kSBar + 8 * kStages);
   if (threadIdx.x == 0)
     for (int s = 0; s < kStages; ++s) mbar_init(bars + s, 1);
-  if (threadIdx.x < 32) tmem_alloc(slot, 64);
+  if (threadIdx.x < 32) tmem_alloc(slot, 64 * kAccumulators);
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
   const uint32_t tmem = *slot;
-  const uint32_t lane = (threadIdx.x / 32) * 32;
+  const int used = a.chunks < kAccumulators ? a.chunks : kAccumulators;
+  const Slot me;
+  const uint32_t r = me.row;
   const uint32_t base = smem_u32(smem);
-  const uint32_t r = threadIdx.x;
   const int64_t tiles = (a.edges + kTile - 1) / kTile;
   const int chunks = a.chunks;
   // Flattened (tile, chunk) sequence of this CTA.
@@ -347,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1) radial_w4_adjoint_kernel(RadialAr
     // Split A in place: hi (TF32-rounded) stays, lo goes to the A-lo buffer.
     unsigned char* st = smem + s * kStageBytes;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < 1024 / kThreads; ++i) {
       const uint32_t off = (threadIdx.x + kThreads * i) * 16;
       float4 v = *reinterpret_cast<float4*>(st + off);
       float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
@@ -357,13 +524,14 @@ __global__ void __launch_bounds__(kThreads, 1) radial_w4_adjoint_kernel(RadialAr
     fence_async_smem();
     fence_before_sync();
     __syncthreads();
-    if (r == 0) {
+    if (threadIdx.x == 0) {
       fence_after_sync();
       const uint32_t sa = base + s * kStageBytes;
+      const uint32_t acc = tmem + 64 * (chunk % kAccumulators);
 #pragma unroll
       for (uint32_t kk = 0; kk < 4; ++kk)
-        mma_tf32x3(tmem, sa + kk * 32, sa + 16384 + kk * 32, sa + 32768 + kk * 32, sa + 32768 + 8192 + kk * 32,
-                   idesc_tf32(kTile, kHidden), (chunk > 0 || kk > 0) ? 1u : 0u);
+        mma_tf32x3(acc, sa + kk * 32, sa + 16384 + kk * 32, sa + 32768 + kk * 32, sa + 32768 + 8192 + kk * 32,
+                   idesc_tf32(kTile, kHidden), (chunk >= kAccumulators || kk > 0) ? 1u : 0u);
       mma_commit(bars + s);
     }
     pending |= 1u << s;
@@ -379,10 +547,16 @@ __global__ void __launch_bounds__(kThreads, 1) radial_w4_adjoint_kernel(RadialAr
       }
       fence_after_sync();
       const int64_t e = item_tile(q) * kTile + r;
-#pragma unroll
-      for (int qq = 0; qq < 4; ++qq) {
+      {
+        const uint32_t qq = me.slice;
         float v[16];
-        tmem_load16(tmem + (lane << 16) + 16 * qq, v);
+        tmem_load16(tmem + me.lane_base + 16 * qq, v);
+        for (int j = 1; j < used; ++j) {
+          float w[16];
+          tmem_load16(tmem + me.lane_base + 64 * j + 16 * qq, w);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] += w[i];
+        }
         if (e < a.edges) {
           float4* dst = reinterpret_cast<float4*>(a.out_h3 + e * kHidden + 16 * qq);
           dst[0] = make_float4(v[0], v[1], v[2], v[3]);
@@ -403,7 +577,7 @@ __global__ void __launch_bounds__(kThreads, 1) radial_w4_adjoint_kernel(RadialAr
   __syncthreads();
   if (threadIdx.x < 32) {
     fence_after_sync();
-    tmem_dealloc(tmem, 64);
+    tmem_dealloc(tmem, 64 * kAccumulators);
   }
 }
 
@@ -426,87 +600,82 @@ __global__ void __launch_bounds__(kThreads, 1) radial_chain_kernel(RadialArgs a)
   __syncthreads();
   fence_after_sync();
   const uint32_t tmem = *slot;
-  const uint32_t lane = (threadIdx.x / 32) * 32;
+  const Slot me;
+  const uint32_t r = me.row;
   const uint32_t base = smem_u32(smem);
-  const uint32_t r = threadIdx.x;
-  const uint32_t trow = tmem + (lane << 16);
+  const uint32_t trow = tmem + me.lane_base;
+  const uint32_t col = 16 * me.slice;                // this thread's 16 columns
   uint32_t phase = 0;
   const int64_t tiles = (a.edges + kTile - 1) / kTile;
   const uint32_t id64 = idesc_tf32(kTile, kHidden);
+  bool ok = true;
 
   auto issue = [&](auto&& body) {
     fence_async_smem();
     fence_before_sync();
     __syncthreads();
-    if (r == 0) {
+    if (threadIdx.x == 0) {
       fence_after_sync();
       body();
       mma_commit(bar);
     }
   };
 
-  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+  for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
     const int64_t e = t * kTile + r;
-    put_features(smem + kSH, a, e, r);
+    if (me.slice == 0) put_features(smem + kSH, a, e, r);
     issue([&] { gemm_layer1(tmem, base + kSH, base + kOffW1); });
-    bool ok = wait_all(bar, phase, a.status);
+    ok = wait_all(bar, phase, a.status);
     // Forward recompute: keep s*silu'(a_l) in TMEM columns 64 + 64*l.
     for (int layer = 0; ok && layer < 3; ++layer) {
+      float v[16], d[16];
+      tmem_load16(trow + col, v);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float v[16], d[16];
-        tmem_load16(trow + 16 * q, v);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          d[i] = silu_scaled_grad(v[i]);
-          v[i] = silu_scaled(v[i]);
-        }
-        tmem_store16(trow + 64 + 64 * layer + 16 * q, d);
-        if (layer < 2) put_operand16(smem + kSH, r, 16 * q, v);
+      for (int i = 0; i < 16; ++i) {
+        d[i] = silu_scaled_grad(v[i]);
+        v[i] = silu_scaled(v[i]);
       }
+      tmem_store16(trow + 64 + 64 * layer + col, d);
       if (layer < 2) {
+        put_operand16(smem + kSH, r, col, v);
         issue([&] { gemm_k64(tmem, base + kSH, base + (layer == 0 ? kOffW2 : kOffW3), kHidden, id64); });
         ok = wait_all(bar, phase, a.status);
       }
     }
     if (!ok) break;
     // da3 = dh3 * s*silu'(a3)
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    {
       float v[16], d[16];
-      tmem_load16(trow + 192 + 16 * q, d);
+      tmem_load16(trow + 192 + col, d);
 #pragma unroll
       for (int i = 0; i < 16; i += 4) {
-        float4 g = e < a.edges ? __ldg(reinterpret_cast<const float4*>(a.grad_h3 + e * kHidden + 16 * q + i))
+        float4 g = e < a.edges ? __ldg(reinterpret_cast<const float4*>(a.grad_h3 + e * kHidden + col + i))
                                : make_float4(0.f, 0.f, 0.f, 0.f);
         v[i] = g.x * d[i];
         v[i + 1] = g.y * d[i + 1];
         v[i + 2] = g.z * d[i + 2];
         v[i + 3] = g.w * d[i + 3];
       }
-      put_operand16(smem + kSH, r, 16 * q, v);
+      put_operand16(smem + kSH, r, col, v);
     }
     // dh2 = da3 W3, da2 = dh2 * s2; dh1 = da2 W2, da1 = dh1 * s1.
     for (int layer = 1; ok && layer >= 0; --layer) {
       issue([&] { gemm_k64(tmem, base + kSH, base + (layer == 1 ? kOffW3T : kOffW2T), kHidden, id64); });
       ok = wait_all(bar, phase, a.status);
       if (!ok) break;
+      float v[16], d[16];
+      tmem_load16(trow + col, v);
+      tmem_load16(trow + 64 + 64 * layer + col, d);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float v[16], d[16];
-        tmem_load16(trow + 16 * q, v);
-        tmem_load16(trow + 64 + 64 * layer + 16 * q, d);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] *= d[i];
-        put_operand16(smem + kSH, r, 16 * q, v);
-      }
+      for (int i = 0; i < 16; ++i) v[i] *= d[i];
+      put_operand16(smem + kSH, r, col, v);
     }
     if (!ok) break;
     // df = da1 W1 (N = 16, columns >= F are zero).
     issue([&] { gemm_k64(tmem, base + kSH, base + kOffW1T, 16, idesc_tf32(kTile, 16)); });
     ok = wait_all(bar, phase, a.status);
     if (!ok) break;
-    {
+    if (me.slice == 0) {
       float v[16];
       tmem_load16(trow, v);
       if (e < a.edges)
@@ -515,6 +684,7 @@ __global__ void __launch_bounds__(kThreads, 1) radial_chain_kernel(RadialArgs a)
     fence_before_sync();
     __syncthreads();
   }
+  if (!ok) mbar_wait(bar, phase, kWaitNs);
   fence_before_sync();
   __syncthreads();
   if (threadIdx.x < 32) {
@@ -527,10 +697,6 @@ __global__ void __launch_bounds__(kThreads, 1) radial_chain_kernel(RadialArgs a)
 // Host side
 // ---------------------------------------------------------------------------
 
-template <int NC>
-constexpr uint32_t forward_smem() {
-  return kOffW3T + NC * 512 + 65536 + 64 + 1024;
-}
 constexpr uint32_t kAdjointSmem = kStages * kStageBytes + 8 * kStages + 64 + 1024;
 constexpr uint32_t kChainSmem = kHiddenImage + 65536 + 64 + 1024;
 
@@ -552,16 +718,15 @@ int prepare_kernel(K kernel, uint32_t smem) {
   return ICTC_OK;
 }
 
-template <int NC>
+static_assert(kFwdSmem <= 232448, "forward shared memory");
+static_assert(sizeof(FwdBars) <= 256, "forward barrier block");
+static_assert(kFwdBar % 8 == 0, "barrier alignment");
+
 int launch_forward(const RadialArgs& a, cudaStream_t s) {
-  constexpr uint32_t smem = forward_smem<NC>();
-  static_assert(forward_smem<NC>() <= 232448, "forward shared memory");
-  if (int st = prepare_kernel(radial_forward_kernel<NC>, smem)) return st;
+  if (int st = prepare_kernel(radial_forward_kernel, kFwdSmem)) return st;
   const int64_t tiles = (a.edges + kTile - 1) / kTile;
-  int per_group = sm_count() / a.groups;
-  if (per_group < 1) per_group = 1;
-  if (per_group > tiles) per_group = (int)tiles;
-  radial_forward_kernel<NC><<<a.groups * per_group, kThreads, smem, s>>>(a);
+  const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
+  radial_forward_kernel<<<grid, kFwdThreads, kFwdSmem, s>>>(a);
   return ICTC_OK;
 }
 
@@ -603,7 +768,7 @@ extern "C" int ictc_radial_pack(const float* w1, const float* w2, const float* w
                                 int hidden, int gates, void* image, int64_t image_bytes) {
   RadialShape s;
   if (!radial_shape(features, hidden, gates, &s)) {
-    ictc_set_error("ictc_radial_pack: unsupported shape (F <= 8, hidden 64, gates a multiple of 32)%s", "");
+    ictc_set_error("ictc_radial_pack: unsupported shape (F <= 8, hidden 64, gates a multiple of 64)%s", "");
     return ICTC_ERR_UNSUPPORTED;
   }
   if (!w1 || !w2 || !w3 || !w4 || !image || image_bytes < (int64_t)s.total) {
@@ -626,10 +791,10 @@ extern "C" int ictc_radial_pack(const float* w1, const float* w2, const float* w
   pack_square(img + kOffW3T, H, [&](uint32_t n, uint32_t k) { return w3[k * H + n]; });
   pack_square(img + kOffW2T, H, [&](uint32_t n, uint32_t k) { return w2[k * H + n]; });
   pack_square(img + kOffW1T, 16, [&](uint32_t n, uint32_t k) { return (int)n < F ? w1[k * F + n] : 0.f; });
-  // W4 [G, 64] in forward column groups of nc rows.
-  for (int g = 0; g < s.groups; ++g)
-    pack_square(img + s.w4 + (uint64_t)g * s.nc * 512, s.nc,
-                [&](uint32_t n, uint32_t k) { return w4[(uint64_t)(g * s.nc + n) * H + k]; });
+  // W4 [G, 64] for the forward in chunks of 64 rows (32 KB each).
+  for (int c = 0; c < gates / kW4Rows; ++c)
+    pack_square(img + s.w4 + (uint64_t)c * kW4Chunk, kW4Rows,
+                [&](uint32_t n, uint32_t k) { return w4[(uint64_t)(kW4Rows * c + n) * H + k]; });
   // W4^T chunks for the adjoint: chunk c = rows n (64) x k in [32c, 32c+32).
   for (int c = 0; c < s.chunks; ++c) {
     unsigned char* chunk = img + s.w4t + (uint64_t)c * 16384;
@@ -664,19 +829,9 @@ extern "C" int ictc_radial_forward(const void* image, const float* feats, float*
   a.edges = edges;
   a.features = features;
   a.gates_width = gates_width;
-  a.nc = s.nc;
-  a.groups = s.groups;
   a.chunks = s.chunks;
   cudaStream_t st = (cudaStream_t)stream;
-  int rc;
-  switch (s.nc) {
-    case 176: rc = launch_forward<176>(a, st); break;
-    case 160: rc = launch_forward<160>(a, st); break;
-    case 128: rc = launch_forward<128>(a, st); break;
-    case 96: rc = launch_forward<96>(a, st); break;
-    case 64: rc = launch_forward<64>(a, st); break;
-    default: rc = launch_forward<32>(a, st); break;
-  }
+  const int rc = launch_forward(a, st);
   if (rc) return rc;
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) {
@@ -710,8 +865,6 @@ extern "C" int ictc_radial_backward(const void* image, const float* feats, const
   a.edges = edges;
   a.features = features;
   a.gates_width = gates_width;
-  a.nc = s.nc;
-  a.groups = s.groups;
   a.chunks = s.chunks;
   cudaStream_t st = (cudaStream_t)stream;
   if (int rc = prepare_kernel(radial_w4_adjoint_kernel, kAdjointSmem)) return rc;

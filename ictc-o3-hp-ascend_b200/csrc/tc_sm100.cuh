@@ -70,6 +70,23 @@ __device__ __forceinline__ void mma_tf32x3(uint32_t d_tmem, uint32_t a_hi, uint3
   mma_tf32(d_tmem, sw128_desc(a_lo), sw128_desc(b_hi), idesc, 1u);
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T: A's rows are the TMEM lanes, one fp32 K value per column.
+__device__ __forceinline__ void mma_tf32_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                            uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+
+// 3xTF32 step with A in TMEM (hi and lo column blocks) and B in shared memory.
+__device__ __forceinline__ void mma_tf32x3_ta(uint32_t d_tmem, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi,
+                                              uint32_t b_lo, uint32_t idesc, uint32_t acc) {
+  mma_tf32_ta(d_tmem, a_hi, sw128_desc(b_hi), idesc, acc);
+  mma_tf32_ta(d_tmem, a_hi, sw128_desc(b_lo), idesc, 1u);
+  mma_tf32_ta(d_tmem, a_lo, sw128_desc(b_hi), idesc, 1u);
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
@@ -101,17 +118,105 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
+// Blocking probe: the thread is suspended in hardware until the phase completes or
+// a short system-defined time passes (then it returns false).
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0u;
+}
+
 // Wait for the phase with the given parity to complete; false after `limit_ns`
-// nanoseconds (or an absolute spin cap), so a lost arrival cannot hang the GPU.
+// nanoseconds (or an absolute probe cap), so a lost arrival cannot hang the GPU.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
-  if (mbar_test(bar, parity)) return true;
+  if (mbar_try(bar, parity)) return true;
   const uint64_t start = global_ns();
-  for (uint32_t spin = 1; spin < (1u << 30); ++spin) {
-    if (mbar_test(bar, parity)) return true;
+  for (uint32_t spin = 1; spin < (1u << 28); ++spin) {
+    if (mbar_try(bar, parity)) return true;
     if ((spin & 63u) == 0u && global_ns() - start > limit_ns) return false;
-    if (spin > 32u) __nanosleep(64);
   }
   return false;
+}
+
+// As mbar_wait, but also gives up as soon as `*abort` is non-zero (another thread
+// of the CTA timed out), so one lost arrival ends the whole CTA quickly.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, uint64_t limit_ns,
+                                                   volatile int* abort) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t start = global_ns();
+  for (uint32_t spin = 1; spin < (1u << 28); ++spin) {
+    if (mbar_try(bar, parity)) return true;
+    if ((spin & 15u) == 0u) {
+      if (*abort) return false;
+      if (global_ns() - start > limit_ns) {
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+  *abort = 1;
+  return false;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// One arrival that also announces `bytes` of bulk-copy data the phase must wait for.
+__device__ __forceinline__ void mbar_arrive_expect(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+// Bulk copy global -> shared (16-byte aligned, size a multiple of 16), completing on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Barrier among `count` threads (a multiple of 32) of the CTA, id 1..15.
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Barrier among `count` threads that also ANDs `pred` over them (uniform result).
+__device__ __forceinline__ bool named_barrier_all(uint32_t id, uint32_t count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(count)
+      : "memory");
+  return r != 0u;
+}
+
+// 8 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_load8(uint32_t taddr, float* v) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_store8(uint32_t taddr, const float* v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+               "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+               "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+               "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
+               : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // TMEM allocation (whole warp).  `slot` receives the base address.
@@ -138,6 +243,21 @@ __device__ __forceinline__ void tmem_load16(uint32_t taddr, float* v) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
+
+// tcgen05.st without waiting; tmem_store_wait() completes every store of the thread.
+__device__ __forceinline__ void tmem_store16_async(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_store_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void tmem_store16(uint32_t taddr, const float* v) {
   asm volatile(

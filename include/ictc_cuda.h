@@ -214,7 +214,7 @@ int ictc_neighbor_fill_receivers(const float* pos, int64_t atoms, int64_t receiv
  * Fused radial MLP of the MACE interaction (tcgen05 tensor cores, 3xTF32):
  *   gates = W4 s*silu(W3 s*silu(W2 s*silu(W1 f)))     (bias-free, s = 1.6791767923989418)
  * for edge embeddings f [E, F] (F <= 8), hidden width 64 and G gate columns
- * (a multiple of 32).  Replaces the radial network `fc` evaluated per edge in
+ * (a multiple of 64).  Replaces the radial network `fc` evaluated per edge in
  * mace_ictc/models/pure_cartesian_ictd_fix.py:1545-1553 (the gates of
  * radial_graph_message, ictc_o3/backends/ascend/capacity_message.py:109-179).
  *   ictc_radial_image_bytes: size of the packed weight image (-1 if unsupported).

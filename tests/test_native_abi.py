@@ -96,11 +96,10 @@ def test_radial_weight_image_round_trips():
         for k in range(0, H, 3):
             check(8192 + 4 * 32768, 16, w1[k, n], n, k)
     w4_base = 8192 + 4 * 32768 + 8192
-    nc = 96                                     # largest supported group width dividing 192
-    for g in range(G // nc):
-        for n in range(0, nc, 11):
+    for c in range(G // 64):                    # forward chunks of 64 rows, 32 KB each
+        for n in range(0, 64, 5):
             for k in range(0, H, 9):
-                check(w4_base + g * nc * 512, nc, w4[g * nc + n, k], n, k)
+                check(w4_base + c * 32768, 64, w4[64 * c + n, k], n, k)
     w4t_base = w4_base + G * 512
     for c in range(G // 32):
         for n in range(0, H, 13):
@@ -122,4 +121,5 @@ def test_radial_rejects_unsupported_shapes():
     assert lib.ictc_radial_image_bytes(9, 64, 192) == -1
     assert lib.ictc_radial_image_bytes(8, 32, 192) == -1
     assert lib.ictc_radial_image_bytes(8, 64, 100) == -1
+    assert lib.ictc_radial_image_bytes(8, 64, 96) == -1
     assert lib.ictc_radial_forward(None, None, None, 10, 8, 64, 192, None, None) == -1
