@@ -151,4 +151,9 @@ __device__ __forceinline__ void store_vec(float* __restrict__ dst, const float (
   }
 }
 
+// Bring one 128-byte line into L1 ahead of its use.
+__device__ __forceinline__ void prefetch_l1(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
 }  // namespace ictc

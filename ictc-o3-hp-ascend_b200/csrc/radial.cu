@@ -10,7 +10,7 @@
 //   control thread issuing MMAs and bulk copies, a hidden-layer warp group and an
 //   output warp group); the hidden activations stay on chip and W4 streams from L2.
 // radial_w4_adjoint_kernel: dh3 = dgates W4, a streaming GEMM over K = G with a
-//   4-stage cp.async pipeline (dgates from HBM, W4^T chunks from L2).
+//   4-stage cp.async pipeline two chunks deep (dgates from HBM, W4^T chunks from L2).
 // radial_chain_kernel: recomputes the hidden layers, keeps s*silu'(a_l) in TMEM and
 //   runs the chain dh3 -> da3 -> dh2 -> ... -> df.
 //
@@ -485,15 +485,16 @@ __global__ void __launch_bounds__(kThreads, 1) radial_w4_adjoint_kernel(RadialAr
   auto item_tile = [&](int64_t q) { return blockIdx.x + (q / chunks) * gridDim.x; };
   bool ok = true;
 
-  for (int64_t q = 0; q < kStages - 1; ++q) {
+  for (int64_t q = 0; q < kStages - 2; ++q) {
     if (q < total) issue_chunk(a, base + (uint32_t)(q % kStages) * kStageBytes, item_tile(q), (int)(q % chunks));
     cp_async_commit();
   }
   for (int64_t q = 0; q < total && ok; ++q) {
     const uint32_t s = (uint32_t)(q % kStages);
     const int chunk = (int)(q % chunks);
-    // Refill the stage read by MMA q-1 with item q + kStages - 1 once that MMA is done.
-    const int64_t next = q + kStages - 1;
+    // Refill the stage read by MMA q-2 with item q + kStages - 2 (that MMA is done or
+    // nearly; the MMA issued one step ago keeps running meanwhile).
+    const int64_t next = q + kStages - 2;
     if (next < total) {
       const uint32_t ns = (uint32_t)(next % kStages);
       if (pending & (1u << ns)) {
@@ -509,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1) radial_w4_adjoint_kernel(RadialAr
       issue_chunk(a, base + ns * kStageBytes, item_tile(next), (int)(next % chunks));
     }
     cp_async_commit();
-    cp_async_wait<kStages - 1>();
+    cp_async_wait<kStages - 2>();
     __syncthreads();
     // Split A in place: hi (TF32-rounded) stays, lo goes to the A-lo buffer.
     unsigned char* st = smem + s * kStageBytes;

@@ -422,6 +422,23 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
         const int64_t e = __shfl_sync(0xffffffffu, e_lane, t);
         const int64_t d = __shfl_sync(0xffffffffu, d_lane, t);
         const float m = __shfl_sync(0xffffffffu, m_lane, t);
+        {
+          // Pull the next edge's gathered output-gradient row and gate row into L1
+          // while this edge computes; the group's slices split the lines.
+          const int tn = t + 1 < batch ? t + 1 : t;
+          const int64_t en = __shfl_sync(0xffffffffu, e_lane, tn);
+          const int64_t dn = __shfl_sync(0xffffffffu, d_lane, tn);
+          if (t + 1 < batch) {
+            const char* grow_n = reinterpret_cast<const char*>(a.grad_out + dn * (int64_t)PS::ROWS * C);
+            const int bytes = PS::ROWS * C * 4;
+            for (int off = (s * 32 + lane) * 128; off < bytes; off += slices * 32 * 128) prefetch_l1(grow_n + off);
+            if (a.gates) {
+              const char* gate_n = reinterpret_cast<const char*>(a.gates + en * (int64_t)PS::NP * C);
+              for (int off = (s * 32 + lane) * 128; off < PS::NP * C * 4; off += slices * 32 * 128)
+                prefetch_l1(gate_n + off);
+            }
+          }
+        }
         if (lane < B) s_y[lane] = __ldg(a.harmonics + e * B + lane);
         __syncwarp();
         build_bond<PS>(s_coef, s_desc, s_y, s_bond, lane);
