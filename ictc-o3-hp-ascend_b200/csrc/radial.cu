@@ -430,7 +430,7 @@ constexpr uint32_t kStageBytes = 3 * 16384;  // A hi, A lo, B (W4^T chunk hi+lo)
 // K chunks rotate over independent TMEM accumulators, summed in FP32 at the end:
 // the tensor core's accumulation error grows with the K it sums, and G reaches
 // thousands.
-constexpr int kAccumulators = 8;
+constexpr int kAccumulators = 4;
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
@@ -459,126 +459,175 @@ __device__ __forceinline__ void issue_chunk(const RadialArgs& a, uint32_t stage,
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1) radial_w4_adjoint_kernel(RadialArgs a) {
+// Warp-specialised: warp 0 lane 0 issues the MMAs; warps 4..19 (the workers) load
+// dgates rows and W4^T chunks with cp.async, split dgates into hi/lo in place, and
+// write dh3.  Two sets of kAccumulators TMEM accumulators alternate between tiles
+// so a tile's MMAs can start while the previous tile's dh3 is written.
+constexpr int kAdjThreads = 640, kWorkers = 512;
+
+struct AdjBars {
+  uint64_t split_done[kStages], mma_done[kStages], acc_full[2], acc_free[2];
+  uint32_t tmem_slot;
+  int abort;
+};
+
+__global__ void __launch_bounds__(kAdjThreads, 1) radial_w4_adjoint_kernel(RadialArgs a) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = aligned_smem(smem_raw);
-  constexpr uint32_t kSBar = kStages * kStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSBar);
-  uint32_t* slot = reinterpret_cast<uint32_t*>(smem + kSBar + 8 * kStages);
-  if (threadIdx.x == 0)
-    for (int s = 0; s < kStages; ++s) mbar_init(bars + s, 1);
-  if (threadIdx.x < 32) tmem_alloc(slot, 64 * kAccumulators);
+  AdjBars* b = reinterpret_cast<AdjBars*>(smem + kStages * kStageBytes);
+  volatile int* abort = &b->abort;
+  const uint32_t warp = threadIdx.x / 32;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&b->split_done[i], 1);
+      mbar_init(&b->mma_done[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&b->acc_full[i], 1);
+      mbar_init(&b->acc_free[i], 1);
+    }
+    b->abort = 0;
+  }
+  if (warp == 0) tmem_alloc(&b->tmem_slot, 512);
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
-  const uint32_t tmem = *slot;
-  const int used = a.chunks < kAccumulators ? a.chunks : kAccumulators;
-  const Slot me;
-  const uint32_t r = me.row;
+  const uint32_t tmem = b->tmem_slot;
   const uint32_t base = smem_u32(smem);
   const int64_t tiles = (a.edges + kTile - 1) / kTile;
   const int chunks = a.chunks;
-  // Flattened (tile, chunk) sequence of this CTA.
+  const int used = chunks < kAccumulators ? chunks : kAccumulators;
   const int64_t my_tiles = tiles > blockIdx.x ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const int64_t total = my_tiles * chunks;
-  uint32_t phases = 0, pending = 0;
   auto item_tile = [&](int64_t q) { return blockIdx.x + (q / chunks) * gridDim.x; };
-  bool ok = true;
 
-  for (int64_t q = 0; q < kStages - 2; ++q) {
-    if (q < total) issue_chunk(a, base + (uint32_t)(q % kStages) * kStageBytes, item_tile(q), (int)(q % chunks));
-    cp_async_commit();
-  }
-  for (int64_t q = 0; q < total && ok; ++q) {
-    const uint32_t s = (uint32_t)(q % kStages);
-    const int chunk = (int)(q % chunks);
-    // Refill the stage read by MMA q-2 with item q + kStages - 2 (that MMA is done or
-    // nearly; the MMA issued one step ago keeps running meanwhile).
-    const int64_t next = q + kStages - 2;
-    if (next < total) {
-      const uint32_t ns = (uint32_t)(next % kStages);
-      if (pending & (1u << ns)) {
-        const bool done = mbar_wait(bars + ns, (phases >> ns) & 1u, kWaitNs);
-        phases ^= 1u << ns;
-        pending &= ~(1u << ns);
-        if (__syncthreads_and(done) == 0) {
-          if (threadIdx.x == 0) flag_error(a.status, 2);
-          ok = false;
-          break;
-        }
-      }
-      issue_chunk(a, base + ns * kStageBytes, item_tile(next), (int)(next % chunks));
-    }
-    cp_async_commit();
-    cp_async_wait<kStages - 2>();
-    __syncthreads();
-    // Split A in place: hi (TF32-rounded) stays, lo goes to the A-lo buffer.
-    unsigned char* st = smem + s * kStageBytes;
-#pragma unroll
-    for (int i = 0; i < 1024 / kThreads; ++i) {
-      const uint32_t off = (threadIdx.x + kThreads * i) * 16;
-      float4 v = *reinterpret_cast<float4*>(st + off);
-      float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
-      *reinterpret_cast<float4*>(st + off) = h;
-      *reinterpret_cast<float4*>(st + 16384 + off) = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
-    }
-    fence_async_smem();
-    fence_before_sync();
-    __syncthreads();
+  if (warp == 0) {
     if (threadIdx.x == 0) {
-      fence_after_sync();
-      const uint32_t sa = base + s * kStageBytes;
-      const uint32_t acc = tmem + 64 * (chunk % kAccumulators);
+      // ----- MMA issue -----
+      uint32_t split_phase[kStages] = {}, free_phase[2] = {};
+      bool ok = true;
+      for (int64_t q = 0; q < total && ok; ++q) {
+        const int s = (int)(q % kStages), chunk = (int)(q % chunks);
+        const int64_t ti = q / chunks;
+        const uint32_t buf = (uint32_t)(ti & 1);
+        if (chunk == 0 && ti >= 2) {
+          ok = mbar_wait_or_abort(&b->acc_free[buf], free_phase[buf], kWaitNs, abort);
+          free_phase[buf] ^= 1u;
+          if (!ok) break;
+        }
+        ok = mbar_wait_or_abort(&b->split_done[s], split_phase[s], kWaitNs, abort);
+        split_phase[s] ^= 1u;
+        if (!ok) break;
+        fence_after_sync();
+        const uint32_t sa = base + s * kStageBytes;
+        const uint32_t acc = tmem + 256 * buf + 64 * (chunk % kAccumulators);
 #pragma unroll
-      for (uint32_t kk = 0; kk < 4; ++kk)
-        mma_tf32x3(acc, sa + kk * 32, sa + 16384 + kk * 32, sa + 32768 + kk * 32, sa + 32768 + 8192 + kk * 32,
-                   idesc_tf32(kTile, kHidden), (chunk >= kAccumulators || kk > 0) ? 1u : 0u);
-      mma_commit(bars + s);
-    }
-    pending |= 1u << s;
-    if (chunk == chunks - 1) {
-      // Tile done: wait for its last MMA, then write dh3.
-      const bool done = mbar_wait(bars + s, (phases >> s) & 1u, kWaitNs);
-      phases ^= 1u << s;
-      pending &= ~(1u << s);
-      if (__syncthreads_and(done) == 0) {
-        if (threadIdx.x == 0) flag_error(a.status, 3);
-        ok = false;
-        break;
+        for (uint32_t kk = 0; kk < 4; ++kk)
+          mma_tf32x3(acc, sa + kk * 32, sa + 16384 + kk * 32, sa + 32768 + kk * 32, sa + 32768 + 8192 + kk * 32,
+                     idesc_tf32(kTile, kHidden), (chunk >= kAccumulators || kk > 0) ? 1u : 0u);
+        mma_commit(&b->mma_done[s]);
+        if (chunk == chunks - 1) mma_commit(&b->acc_full[buf]);
       }
-      fence_after_sync();
-      const int64_t e = item_tile(q) * kTile + r;
-      {
-        const uint32_t qq = me.slice;
+    }
+  } else if (warp >= 4) {
+    // ----- workers: 16 warps; epilogue slot = quadrant warp % 4, 16-column slice (warp - 4) / 4 -----
+    const uint32_t wt = threadIdx.x - 128;           // 0 .. 511
+    const uint32_t row = (warp % 4) * 32 + threadIdx.x % 32;
+    const uint32_t slice = (warp - 4) / 4;
+    const uint32_t lanes = tmem + (((warp % 4) * 32) << 16);
+    uint32_t done_phase[kStages] = {}, full_phase[2] = {};
+    bool ok = true;
+    auto issue = [&](int64_t q) {
+      const uint32_t stage = base + (uint32_t)(q % kStages) * kStageBytes;
+      const int64_t tile = item_tile(q);
+      const int chunk = (int)(q % chunks);
+#pragma unroll
+      for (int i = 0; i < 1024 / kWorkers; ++i) {
+        const uint32_t idx = wt + kWorkers * i;
+        const uint32_t r = idx / 8, ch = idx % 8;
+        const int64_t e = tile * kTile + r;
+        const bool valid = e < a.edges;
+        const float* src = valid ? a.grad_gates + e * a.gates_width + chunk * 32 + ch * 4 : a.grad_gates;
+        cp_async16(stage + sw128_chunk(r, ch), src, valid ? 16u : 0u);
+      }
+      const unsigned char* img = a.image + kOffW4 + (uint64_t)a.gates_width * 512u + (uint64_t)chunk * 16384u;
+#pragma unroll
+      for (int i = 0; i < 1024 / kWorkers; ++i) {
+        const uint32_t idx = wt + kWorkers * i;
+        cp_async16(stage + 2 * 16384 + idx * 16, img + idx * 16, 16u);
+      }
+    };
+    for (int64_t q = 0; q < kStages - 2; ++q) {
+      if (q < total) issue(q);
+      cp_async_commit();
+    }
+    for (int64_t q = 0; q < total && ok; ++q) {
+      const int s = (int)(q % kStages), chunk = (int)(q % chunks);
+      const int64_t next = q + kStages - 2;          // reuses the stage of item q - 2
+      if (next < total) {
+        if (q >= 2) {
+          const int ns = (int)(next % kStages);
+          ok = named_barrier_all(1, kWorkers, mbar_wait_or_abort(&b->mma_done[ns], done_phase[ns], kWaitNs, abort));
+          done_phase[ns] ^= 1u;
+          if (!ok) break;
+        }
+        issue(next);
+      }
+      cp_async_commit();
+      cp_async_wait<kStages - 2>();
+      named_barrier(1, kWorkers);
+      unsigned char* st = smem + s * kStageBytes;
+#pragma unroll
+      for (int i = 0; i < 1024 / kWorkers; ++i) {
+        const uint32_t off = (wt + kWorkers * i) * 16;
+        float4 v = *reinterpret_cast<float4*>(st + off);
+        float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
+        *reinterpret_cast<float4*>(st + off) = h;
+        *reinterpret_cast<float4*>(st + 16384 + off) = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+      }
+      fence_async_smem();
+      named_barrier(1, kWorkers);
+      if (wt == 0) mbar_arrive(&b->split_done[s]);
+      if (chunk == chunks - 1) {
+        const int64_t ti = q / chunks;
+        const uint32_t buf = (uint32_t)(ti & 1);
+        ok = named_barrier_all(1, kWorkers, mbar_wait_or_abort(&b->acc_full[buf], full_phase[buf], kWaitNs, abort));
+        full_phase[buf] ^= 1u;
+        if (!ok) break;
+        fence_after_sync();
+        const int64_t e = item_tile(q) * kTile + row;
         float v[16];
-        tmem_load16(tmem + me.lane_base + 16 * qq, v);
+        tmem_load16(lanes + 256 * buf + 16 * slice, v);
         for (int j = 1; j < used; ++j) {
           float w[16];
-          tmem_load16(tmem + me.lane_base + 64 * j + 16 * qq, w);
+          tmem_load16(lanes + 256 * buf + 64 * j + 16 * slice, w);
 #pragma unroll
           for (int i = 0; i < 16; ++i) v[i] += w[i];
         }
+        fence_before_sync();
+        named_barrier(1, kWorkers);
+        if (wt == 0) mbar_arrive(&b->acc_free[buf]);
         if (e < a.edges) {
-          float4* dst = reinterpret_cast<float4*>(a.out_h3 + e * kHidden + 16 * qq);
+          float4* dst = reinterpret_cast<float4*>(a.out_h3 + e * kHidden + 16 * slice);
           dst[0] = make_float4(v[0], v[1], v[2], v[3]);
           dst[1] = make_float4(v[4], v[5], v[6], v[7]);
           dst[2] = make_float4(v[8], v[9], v[10], v[11]);
           dst[3] = make_float4(v[12], v[13], v[14], v[15]);
         }
       }
-      fence_before_sync();
-      __syncthreads();
     }
+    cp_async_wait<0>();
   }
-  cp_async_wait<0>();
-  // Drain MMAs still tracked (only after an error), with the same time limit.
-  for (int s = 0; s < kStages; ++s)
-    if (pending & (1u << s)) mbar_wait(bars + s, (phases >> s) & 1u, kWaitNs);
-  fence_before_sync();
   __syncthreads();
-  if (threadIdx.x < 32) {
+  if (threadIdx.x == 0 && *abort) flag_error(a.status, 5);
+  if (warp == 0) {
+    if (threadIdx.x == 0 && *abort) {
+      // After an error, MMAs may still be in flight: wait (bounded) for the last one issued.
+      for (int i = 0; i < kStages; ++i) mbar_wait(&b->mma_done[i], 0, 1000000ull);
+    }
+    __syncwarp();
     fence_after_sync();
-    tmem_dealloc(tmem, 64 * kAccumulators);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -698,7 +747,8 @@ __global__ void __launch_bounds__(kThreads, 1) radial_chain_kernel(RadialArgs a)
 // Host side
 // ---------------------------------------------------------------------------
 
-constexpr uint32_t kAdjointSmem = kStages * kStageBytes + 8 * kStages + 64 + 1024;
+constexpr uint32_t kAdjointSmem = kStages * kStageBytes + 256 + 1024;
+static_assert(sizeof(AdjBars) <= 256, "adjoint barrier block");
 constexpr uint32_t kChainSmem = kHiddenImage + 65536 + 64 + 1024;
 
 int sm_count() {
@@ -872,7 +922,7 @@ extern "C" int ictc_radial_backward(const void* image, const float* feats, const
   if (int rc = prepare_kernel(radial_chain_kernel, kChainSmem)) return rc;
   const int64_t tiles = (edges + kTile - 1) / kTile;
   const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
-  radial_w4_adjoint_kernel<<<grid, kThreads, kAdjointSmem, st>>>(a);
+  radial_w4_adjoint_kernel<<<grid, kAdjThreads, kAdjointSmem, st>>>(a);
   radial_chain_kernel<<<grid, kThreads, kChainSmem, st>>>(a);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) {
