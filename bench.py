@@ -276,7 +276,7 @@ def mace_block(device, steps, warmup, atoms=16384, cpu_seconds=0.0):
         r = vec.norm(dim=1)
         harm = ops.harmonics(vec / r.unsqueeze(-1), L)
         feats = radial_embedding(r, 5.0, 8, 5)
-        message, sc = inter(ops, h, harm, feats, src, dst, None, groups)
+        message, sc = inter(ops, h, harm, feats, src, dst, None, groups, None, species)
         out = prod(ops, message, sc, species)
         energy = readout(out[:, :C]).sum()
         return torch.autograd.grad(energy, [p])[0]

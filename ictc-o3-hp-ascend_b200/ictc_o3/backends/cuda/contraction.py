@@ -89,27 +89,8 @@ def species_tiles(index: torch.Tensor, num_elements: int):
     cached = getattr(index, "_ictc_cuda_sc_tiles", None)
     if cached is not None and cached[0] == key:
         return cached[1]
-    index = index.to(torch.int64)
-    if index.numel():
-        lo, hi = torch.stack((index.min(), index.max())).cpu().tolist()
-        if lo < 0 or hi >= num_elements:
-            raise ValueError("Species index is outside the element table")
-    order = torch.argsort(index, stable=True)
-    counts = torch.bincount(index, minlength=num_elements).cpu().tolist()
-    tiles, species, start = [], [], 0
-    for s, count in enumerate(counts):
-        if count:
-            padded = -(-count // nb) * nb
-            block = torch.full((padded,), -1, dtype=torch.int64, device=index.device)
-            block[:count] = order[start:start + count]
-            tiles.append(block.view(-1, nb))
-            species.append(torch.full((padded // nb,), s, dtype=torch.int32, device=index.device))
-        start += count
-    if tiles:
-        result = (torch.cat(tiles).contiguous(), torch.cat(species).contiguous())
-    else:
-        result = (torch.empty(0, nb, dtype=torch.int64, device=index.device),
-                  torch.empty(0, dtype=torch.int32, device=index.device))
+    from .linear import species_tiles_of
+    result = species_tiles_of(index, num_elements, nb)
     index_ref = index
     try:
         index_ref._ictc_cuda_sc_tiles = (key, result)

@@ -39,14 +39,32 @@ class GraphCSR:
         self.src_order, self.src_offsets = _csr(src, self.src_nodes)
 
 
+def mark_grouped(keys: torch.Tensor, grouped: bool):
+    """Record that ``keys`` is (or is not) non-decreasing, so CSR views skip the check."""
+    keys._ictc_grouped = (keys._version, bool(grouped))
+
+
+def mark_trusted_graph(src, dst, src_nodes, dst_nodes):
+    """Record bounds that the producer of an edge list guarantees (e.g. the neighbour
+    search), so ``validate_graph`` needs no device-to-host read for it."""
+    src._ictc_cuda_graph_bounds = (weakref.ref(dst), (src._version, dst._version, int(src_nodes), int(dst_nodes)))
+
+
 def _csr(keys: torch.Tensor, nodes: int):
-    """(order, offsets); order is None when the edges are already grouped by key."""
-    offsets = torch.zeros(nodes + 1, dtype=torch.int64, device=keys.device)
-    if keys.numel():
-        offsets[1:] = torch.cumsum(torch.bincount(keys, minlength=nodes), 0)
-        if bool((keys[1:] >= keys[:-1]).all()):
-            return None, offsets
-    return torch.argsort(keys, stable=True), offsets
+    """(order, offsets); order is None when the edges are already grouped by key.
+
+    Offsets come from a binary search of the sorted keys (no host synchronisation);
+    the grouping check is skipped for keys marked by their producer."""
+    mark = getattr(keys, "_ictc_grouped", None)
+    if mark is not None and mark[0] == keys._version:
+        grouped = mark[1]
+    else:
+        grouped = keys.numel() == 0 or bool((keys[1:] >= keys[:-1]).all())
+    order = None if grouped else torch.argsort(keys, stable=True)
+    sorted_keys = keys if order is None else keys.index_select(0, order)
+    bounds = torch.arange(nodes + 1, dtype=keys.dtype, device=keys.device)
+    offsets = torch.searchsorted(sorted_keys, bounds)
+    return order, offsets
 
 
 def validate_graph(src, dst, src_nodes, dst_nodes, device):

@@ -43,4 +43,10 @@ def neighbor_list(pos: torch.Tensor, box, cutoff: float, receivers: int = None):
     if edges:
         _native.call("ictc_neighbor_fill_receivers", ptr(pos), int(atoms), rows, box_arr, float(cutoff),
                      ptr(workspace), size, ptr(offsets), ptr(src), ptr(dst), ptr(shift), stream)
+    # The search guarantees bounds and receiver grouping: message CSR views of this
+    # edge list need no device-to-host checks.
+    from .message import mark_grouped, mark_trusted_graph
+    mark_grouped(dst, True)
+    mark_grouped(src, False)
+    mark_trusted_graph(src, dst, atoms, rows)
     return src, dst, shift, offsets

@@ -126,9 +126,13 @@ class ChannelLinearSO3(nn.Module):
                 nn.init.normal_(w, std=1.0 / math.sqrt(max(self.in_channels[l], 1)))
             self.weights.append(nn.Parameter(w))
 
-    def forward(self, x):
+    def forward(self, x, scale: float = 1.0):
+        if x.is_cuda:
+            from ictc_o3.backends.cuda.linear import channel_mix
+            return channel_mix(x, list(self.weights), scale=scale)
         blocks = _blocks(x, self.in_channels, self.lmax)
-        return _merge([torch.matmul(self.weights[l], b) for l, b in enumerate(blocks)])
+        out = _merge([torch.matmul(self.weights[l], b) for l, b in enumerate(blocks)])
+        return out if scale == 1.0 else out * scale
 
 
 class ElementLinearSO3(nn.Module):
@@ -144,7 +148,11 @@ class ElementLinearSO3(nn.Module):
             nn.init.normal_(w, std=1.0 / math.sqrt(channels))
         self.weight = nn.Parameter(w)
 
-    def forward(self, x, groups):
+    def forward(self, x, groups, species=None):
+        if x.is_cuda and species is not None:
+            from ictc_o3.backends.cuda.linear import channel_mix
+            return channel_mix(x, [self.weight[:, l] for l in range(self.lmax + 1)], species=species,
+                               num_elements=self.num_elements)
         blocks = _blocks(x, [self.channels] * (self.lmax + 1), self.lmax)
         outs = []
         for l, b in enumerate(blocks):
@@ -203,18 +211,20 @@ class InteractionBlock(nn.Module):
         self.message_selector = None if use_self_connection else ElementLinearSO3(num_elements, channels, lmax,
                                                                                   init="identity")
 
-    def forward(self, ops, node_feats, edge_harmonics, edge_feats, src, dst, mask, groups, owned=None):
-        """Messages into the first ``owned`` nodes (all nodes by default); ``groups`` index those."""
+    def forward(self, ops, node_feats, edge_harmonics, edge_feats, src, dst, mask, groups, owned=None,
+                species=None):
+        """Messages into the first ``owned`` nodes (all nodes by default); ``groups`` and
+        ``species`` (the owned nodes' species) select the element-conditioned weights."""
         owned = node_feats.shape[0] if owned is None else owned
         x_up = self.linear_up(node_feats)
         radial = getattr(ops, "radial", None)
         gates = radial(self.fc, edge_feats) if radial is not None else self.fc(edge_feats)
         msg = ops.message(self.tp, x_up, edge_harmonics, gates, src, dst, mask, owned)
-        message = self.message_linear(msg) / max(self.avg_num_neighbors, 1e-8)
+        message = self.message_linear(msg, scale=1.0 / max(self.avg_num_neighbors, 1e-8))
         if self.self_connection is None:
-            return self.message_selector(message, groups), None
+            return self.message_selector(message, groups, species), None
         sc_in = node_feats[:owned, :self.channels * (self.sc_lmax + 1) ** 2]
-        return message, self.self_connection(sc_in, groups)
+        return message, self.self_connection(sc_in, groups, species)
 
 
 class ProductBlock(nn.Module):
@@ -298,7 +308,8 @@ class MACEICTC(nn.Module):
         if owned != n_local and exchange is None:
             raise ValueError("ghost rows need an exchange to refresh their features")
         own_species = species if owned == n_local else species[:owned]
-        groups = species_groups(own_species, self.num_elements)
+        # The CUDA linears take species directly; node index groups serve the torch path.
+        groups = None if species.is_cuda else species_groups(own_species, self.num_elements)
         harmonics, feats, mask = self.edge_features(vec)
         h = self.node_embedding.weight.t().index_select(0, species)
         energy = None
@@ -306,7 +317,8 @@ class MACEICTC(nn.Module):
         for layer in range(count):
             if layer and exchange is not None:
                 h = exchange(h)
-            message, sc = self.interactions[layer](self.ops, h, harmonics, feats, src, dst, mask, groups, owned)
+            message, sc = self.interactions[layer](self.ops, h, harmonics, feats, src, dst, mask, groups, owned,
+                                                   own_species)
             h = self.products[layer](self.ops, message, sc, own_species)
             readout = (self.layer_readouts[layer](h[:, :self.channels]) if layer < len(self.interactions) - 1
                        else self.last_readout(h[:, :self.channels]))

@@ -52,38 +52,40 @@ def slab_layout(pos: torch.Tensor, side: float, rank: int, world: int, halo: flo
     width = side / world
     if world > 1 and width < halo:
         raise ValueError("slab width must be at least the halo depth")
-    x = pos[:, 0] - side * torch.floor(pos[:, 0] / side)
-    owner = torch.clamp((x / width).long(), 0, world - 1)
     x0, x1 = rank * width, (rank + 1) * width
-    owned = torch.nonzero(owner == rank).flatten()
-    if world == 1:
+    if world == 1:                                   # every atom is owned; no ghosts
+        owned = torch.arange(pos.shape[0], device=pos.device)
         empty = owned[:0]
         zeros = torch.zeros(owned.numel(), dtype=pos.dtype, device=pos.device)
         return SlabLayout(rank, world, owned.numel(), owned, zeros, empty, empty, slice(owned.numel(), owned.numel()),
                           slice(owned.numel(), owned.numel()), rank, rank, x0, x1)
+    x = pos[:, 0] - side * torch.floor(pos[:, 0] / side)
+    owner = torch.clamp((x / width).long(), 0, world - 1)
     left, right = (rank - 1) % world, (rank + 1) % world
-
-    def rows_within(of_rank, lo, hi):
-        """Atoms owned by ``of_rank`` with (unwrapped) x in [lo, hi), and their x shift."""
-        mask = owner == of_rank
-        xs = x.clone()
-        result, shifts = [], []
-        for s in (-side, 0.0, side):
-            sel = torch.nonzero(mask & (xs + s >= lo) & (xs + s < hi)).flatten()
-            result.append(sel)
-            shifts.append(torch.full((sel.numel(),), s, dtype=pos.dtype, device=pos.device))
-        return torch.cat(result), torch.cat(shifts)
-
-    gl, gl_shift = rows_within(left, x0 - halo, x0)        # my left ghosts (owned by the left rank)
-    gr, gr_shift = rows_within(right, x1, x1 + halo)       # my right ghosts
-    # What I send: my owned atoms within halo of my faces, in the order the neighbour
-    # lists them as ghosts (the same global-index order as rows_within on its side).
-    mine_left, _ = rows_within(rank, x0, x0 + halo)        # right ghosts of my left neighbour
-    mine_right, _ = rows_within(rank, x1 - halo, x1)       # left ghosts of my right neighbour
-    local_of = torch.full((pos.shape[0],), -1, dtype=torch.long, device=pos.device)
+    n = pos.shape[0]
+    # Ghost images sit next to the slab: the left neighbour's atoms within `halo` below
+    # x0 (shifted by -L when the slab touches x = 0), the right neighbour's within
+    # `halo` above x1 (shifted by +L when it touches x = L).  With two ranks one atom
+    # can be both a left and a right ghost (two images), so the sets are separate masks.
+    shift_left = -side if rank == 0 else 0.0
+    shift_right = side if rank == world - 1 else 0.0
+    masks = torch.stack([
+        owner == rank,                                                            # owned
+        (owner == left) & (x + shift_left >= x0 - halo) & (x + shift_left < x0),   # left ghosts
+        (owner == right) & (x + shift_right >= x1) & (x + shift_right < x1 + halo),  # right ghosts
+        (owner == rank) & (x < x0 + halo),                                       # left neighbour's right ghosts
+        (owner == rank) & (x >= x1 - halo),                                      # right neighbour's left ghosts
+    ])
+    counts = masks.sum(1).cpu().tolist()                                         # one device-to-host read
+    flat = torch.nonzero(masks.reshape(-1)).flatten()
+    groups = torch.split(flat, counts)
+    owned, gl, gr, mine_left, mine_right = (g - k * n for k, g in enumerate(groups))  # ascending atom ids
+    local_of = torch.full((n,), -1, dtype=torch.long, device=pos.device)
     local_of[owned] = torch.arange(owned.numel(), device=pos.device)
     local_global = torch.cat([owned, gl, gr])
-    shift = torch.cat([torch.zeros(owned.numel(), dtype=pos.dtype, device=pos.device), gl_shift, gr_shift])
+    shift = torch.cat([torch.zeros(owned.numel(), dtype=pos.dtype, device=pos.device),
+                       torch.full((gl.numel(),), shift_left, dtype=pos.dtype, device=pos.device),
+                       torch.full((gr.numel(),), shift_right, dtype=pos.dtype, device=pos.device)])
     n_own = owned.numel()
     return SlabLayout(rank, world, n_own, local_global, shift, local_of[mine_left], local_of[mine_right],
                       slice(n_own, n_own + gl.numel()), slice(n_own + gl.numel(), n_own + gl.numel() + gr.numel()),

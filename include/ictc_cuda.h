@@ -236,6 +236,22 @@ int ictc_radial_backward(const void* image, const float* feats, const float* gra
                          void* stream);
 
 /*
+ * Equivariant channel mixing of one degree block l (M = 2l+1) in the flat
+ * [channel][M] feature layout, in place in the caller's rows:
+ *   y[n*y_stride + y_offset + o*M + k] (+)= scale * sum_i W_s[o, i] x[n*x_stride + x_offset + i*M + k]
+ * weight: [S, cout, cin]; s = tile_species[t] for the nodes of tile t.
+ * tiles: [num_tiles, ictc_channel_mix_tile_nodes()] node ids (-1 padded), grouped
+ * by species; NULL = contiguous tiles over all `nodes` with species 0.
+ * accumulate: add into y instead of overwriting.  Replaces the per-degree linears
+ * of mace_ictc/models/pure_cartesian_ictd_fix.py:335-392 (channel linears),
+ * :629-661 (message_linear) and :2381-2440 (element-conditioned linears).
+ */
+int ictc_channel_mix_tile_nodes(void);
+int ictc_channel_mix(const float* x, int64_t x_stride, int64_t x_offset, const float* weight, const int64_t* tiles,
+                     const int32_t* tile_species, int64_t num_tiles, float* y, int64_t y_stride, int64_t y_offset,
+                     int64_t nodes, int cin, int cout, int degree, float scale, int accumulate, void* stream);
+
+/*
  * Allocation-free neighbour search.  No counterpart in the reference: it exists
  * for callers that cannot allocate device memory during a step (an MD engine
  * that owns all device buffers in its own pool, or a host program using this C
