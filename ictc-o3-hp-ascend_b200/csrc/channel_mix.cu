@@ -10,11 +10,11 @@
 // (:2381-2440).  It reads and writes the flat feature rows in place, so a linear
 // needs no degree-block slicing, concatenation or layout copies.
 //
-// One CTA: a tile of kTileNodes nodes (contiguous, or species-homogeneous node
-// lists) x 64 output channels.  The reduction over input channels runs in chunks
-// of kChunk: the chunk of W (transposed into shared memory) and the tile's input
-// rows are staged in shared memory; thread (o, g) accumulates its output channel o
-// for the nodes g, g+4, g+8, g+12 of the tile.
+// One CTA: a tile of 32 nodes (contiguous, or a species-homogeneous node list) x
+// 64 output channels.  Lane = node, warp = 8 consecutive output channels: per input
+// channel a thread reads its node's M values (padded rows, no bank conflicts) and
+// the warp's 8 weights as two broadcast float4 loads, for 8*M FMAs.  The reduction
+// over input channels runs in chunks of 32 staged in shared memory.
 #include <cstdint>
 #include <cstdio>
 
@@ -27,10 +27,10 @@ namespace ictc {
 namespace {
 
 constexpr int kOutTile = 64;      // output channels per CTA
-constexpr int kGroups = 4;        // node groups per CTA (256 threads)
-constexpr int kNodesPerThread = 4;
-constexpr int kTileNodes = kGroups * kNodesPerThread;  // 16
-constexpr int kChunk = 64;        // input channels per shared-memory stage
+constexpr int kOutPerWarp = 8;    // output channels per thread (8 warps)
+constexpr int kTileNodes = 32;    // nodes per CTA (lane = node)
+constexpr int kChunk = 32;        // input channels per shared-memory stage
+constexpr int kWStride = kOutTile + 4;  // padded row of the transposed weight chunk
 
 struct MixArgs {
   const float* x;
@@ -47,16 +47,15 @@ struct MixArgs {
 template <int M>
 __global__ void __launch_bounds__(256) channel_mix_kernel(MixArgs a) {
   extern __shared__ __align__(16) float smem[];
-  float* s_w = smem;                               // [kChunk][kOutTile + 1] (padded: no bank conflicts)
-  float* s_x = smem + kChunk * (kOutTile + 1);     // [kTileNodes][kChunk * M]
-  const int tid = threadIdx.x;
-  const int o_local = tid % kOutTile, g = tid / kOutTile;
+  constexpr int kXStride = kChunk * M + 1;        // odd: the 32 node rows hit distinct banks
+  float* s_w = smem;                               // [kChunk][kWStride]: s_w[i][o] = W[o0 + o, i0 + i]
+  float* s_x = smem + kChunk * kWStride;           // [kTileNodes][kXStride]
+  __shared__ int64_t s_node[kTileNodes];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int o0 = blockIdx.y * kOutTile;
-  const int o = o0 + o_local;
+  const int ow = warp * kOutPerWarp;               // this warp's first output channel in the tile
 
   for (int64_t t = blockIdx.x; t < a.num_tiles; t += gridDim.x) {
-    int64_t node[kNodesPerThread];
-    __shared__ int64_t s_node[kTileNodes];
     if (tid < kTileNodes) {
       int64_t n = -1;
       if (a.tiles) {
@@ -68,50 +67,75 @@ __global__ void __launch_bounds__(256) channel_mix_kernel(MixArgs a) {
       s_node[tid] = n;
     }
     __syncthreads();
-#pragma unroll
-    for (int j = 0; j < kNodesPerThread; ++j) node[j] = s_node[g + kGroups * j];
+    const int64_t node = s_node[lane];
     const int species = a.tile_species ? a.tile_species[t] : 0;
     const float* w = a.w + (int64_t)species * a.cout * a.cin;
 
-    float acc[kNodesPerThread][M];
+    float acc[kOutPerWarp][M];
 #pragma unroll
-    for (int j = 0; j < kNodesPerThread; ++j)
+    for (int j = 0; j < kOutPerWarp; ++j)
 #pragma unroll
       for (int k = 0; k < M; ++k) acc[j][k] = 0.f;
 
+    // Register-staged pipeline: the loads of chunk c+1 are in flight while chunk c
+    // is computed from shared memory.
+    constexpr int kWPer = kChunk * kOutTile / 256;               // weight values per thread
+    constexpr int kXPer = kTileNodes * kChunk * M / 256;         // input values per thread
+    float rw[kWPer], rx[kXPer];
+    auto fetch = [&](int i0) {
+      const int kc = min(kChunk, a.cin - i0);
+#pragma unroll
+      for (int q = 0; q < kWPer; ++q) {
+        const int idx = tid + 256 * q, i = idx % kChunk, ol = idx / kChunk;
+        rw[q] = (i < kc && o0 + ol < a.cout) ? __ldg(w + (int64_t)(o0 + ol) * a.cin + i0 + i) : 0.f;
+      }
+#pragma unroll
+      for (int q = 0; q < kXPer; ++q) {
+        const int idx = tid + 256 * q, nl = idx / (kChunk * M), r = idx % (kChunk * M);
+        const int64_t n = s_node[nl];
+        rx[q] = (n >= 0 && r < kc * M) ? __ldg(a.x + n * a.x_stride + a.x_offset + (int64_t)i0 * M + r) : 0.f;
+      }
+    };
+    fetch(0);
     for (int i0 = 0; i0 < a.cin; i0 += kChunk) {
       const int kc = min(kChunk, a.cin - i0);
-      // W chunk, transposed: s_w[i][o_local] = W[o0 + o_local, i0 + i].
-      for (int idx = tid; idx < kChunk * kOutTile; idx += blockDim.x) {
-        const int i = idx % kChunk, ol = idx / kChunk;
-        s_w[i * (kOutTile + 1) + ol] = (i < kc && o0 + ol < a.cout) ? __ldg(w + (int64_t)(o0 + ol) * a.cin + i0 + i) : 0.f;
+#pragma unroll
+      for (int q = 0; q < kWPer; ++q) {
+        const int idx = tid + 256 * q, i = idx % kChunk, ol = idx / kChunk;
+        s_w[i * kWStride + ol] = rw[q];
       }
-      // Input rows of the tile: kc * M contiguous floats per node.
-      for (int idx = tid; idx < kTileNodes * kChunk * M; idx += blockDim.x) {
-        const int nl = idx / (kChunk * M), r = idx % (kChunk * M);
-        const int64_t n = s_node[nl];
-        s_x[idx] = (n >= 0 && r < kc * M) ? __ldg(a.x + n * a.x_stride + a.x_offset + (int64_t)i0 * M + r) : 0.f;
+#pragma unroll
+      for (int q = 0; q < kXPer; ++q) {
+        const int idx = tid + 256 * q, nl = idx / (kChunk * M), r = idx % (kChunk * M);
+        s_x[nl * kXStride + r] = rx[q];
       }
       __syncthreads();
+      if (i0 + kChunk < a.cin) fetch(i0 + kChunk);
+      const float* xr = s_x + lane * kXStride;
 #pragma unroll 4
       for (int i = 0; i < kc; ++i) {
-        const float wv = s_w[i * (kOutTile + 1) + o_local];
+        const float4 w0 = *reinterpret_cast<const float4*>(s_w + i * kWStride + ow);
+        const float4 w1 = *reinterpret_cast<const float4*>(s_w + i * kWStride + ow + 4);
+        const float wv[kOutPerWarp] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        float xv[M];
 #pragma unroll
-        for (int j = 0; j < kNodesPerThread; ++j) {
-          const float* xr = s_x + (g + kGroups * j) * (kChunk * M) + i * M;
+        for (int k = 0; k < M; ++k) xv[k] = xr[i * M + k];
 #pragma unroll
-          for (int k = 0; k < M; ++k) acc[j][k] = fmaf(wv, xr[k], acc[j][k]);
-        }
+        for (int j = 0; j < kOutPerWarp; ++j)
+#pragma unroll
+          for (int k = 0; k < M; ++k) acc[j][k] = fmaf(wv[j], xv[k], acc[j][k]);
       }
       __syncthreads();
     }
-    if (o < a.cout) {
+    if (node >= 0) {
+      float* yr = a.y + node * a.y_stride + a.y_offset;
 #pragma unroll
-      for (int j = 0; j < kNodesPerThread; ++j) {
-        if (node[j] < 0) continue;
-        float* yr = a.y + node[j] * a.y_stride + a.y_offset + (int64_t)o * M;
+      for (int j = 0; j < kOutPerWarp; ++j) {
+        const int o = o0 + ow + j;
+        if (o >= a.cout) break;
 #pragma unroll
-        for (int k = 0; k < M; ++k) yr[k] = a.accumulate ? yr[k] + a.scale * acc[j][k] : a.scale * acc[j][k];
+        for (int k = 0; k < M; ++k)
+          yr[o * M + k] = a.accumulate ? yr[o * M + k] + a.scale * acc[j][k] : a.scale * acc[j][k];
       }
     }
   }
@@ -119,8 +143,8 @@ __global__ void __launch_bounds__(256) channel_mix_kernel(MixArgs a) {
 
 template <int M>
 int launch(const MixArgs& a, cudaStream_t stream) {
-  const size_t smem = sizeof(float) * (kChunk * (kOutTile + 1) + kTileNodes * kChunk * M);
-  static_assert(sizeof(float) * (kChunk * (kOutTile + 1) + kTileNodes * kChunk * 7) <= 48 * 1024,
+  const size_t smem = sizeof(float) * (kChunk * kWStride + kTileNodes * (kChunk * M + 1));
+  static_assert(sizeof(float) * (kChunk * kWStride + kTileNodes * (kChunk * 7 + 1)) <= 48 * 1024,
                 "fits the default dynamic shared memory");
   int device = 0, sms = 0;
   cudaGetDevice(&device);
