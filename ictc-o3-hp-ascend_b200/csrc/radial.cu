@@ -174,35 +174,35 @@ __device__ __forceinline__ unsigned char* aligned_smem(unsigned char* raw) {
 }
 
 // ---------------------------------------------------------------------------
-// Forward (warp-specialised, activations in TMEM)
+// Forward (warp-specialised, activations in TMEM, two MMA issuers)
 //
-//   warp 0, lane 0  control: issues every MMA and the bulk copies of W4 chunks;
+//   warp 0, lane 0  hidden issuer: the three hidden-layer GEMMs of tile i;
+//   warp 1, lane 0  output issuer: the W4 chunk GEMMs of tile i-1 and the bulk
+//                   copies of W4 chunks;
 //   warps 4..11     hidden group: features and s*silu epilogues, written to TMEM;
-//   warps 12..19    output group: gate chunks TMEM -> HBM.
-// TMEM columns: [0,64) hidden accumulator, [64,128) / [128,192) hidden activation
-// hi / lo (the A operand of the next layer), [192,200) / [200,208) features hi / lo,
-// [256,512) four 64-column gate slots.  A operands are read from TMEM, so an MMA
-// only reads its weights from shared memory.
-// Per tile: L1, L2, L3, then G/64 chunk MMAs (h3 x W4 rows of the chunk, N = 64) into
-// the slot ring that the output group drains while the next tile's hidden layers
-// run; the output group stages each chunk in shared memory and writes whole row
-// segments (coalesced).  W4 chunks (32 KB, hi + lo) stream from L2 through a
-// 3-stage shared ring; a stage is refilled once the MMAs that read it two chunks
-// earlier are done.
+//   warps 12..19    output group: gate chunks TMEM -> shared staging -> HBM.
+// TMEM columns: [0,64) hidden accumulator, [64,192) and [192,320) two activation
+// buffers (hi 64 columns, lo 64 columns) used by alternate tiles, [320,336)
+// features hi / lo, [384,512) two 64-column gate slots.  A operands are read from
+// TMEM, so an MMA only reads its weights from shared memory.  With the activation
+// buffers alternating, tile i's hidden chain runs while tile i-1's W4 chunks (and
+// their stores) proceed, and the two issuers keep the tensor pipe fed.  W4 chunks
+// (32 KB, hi + lo) stream from L2 through a 3-stage shared ring; a stage is
+// refilled once the MMAs that read it two chunks earlier are done.
 // ---------------------------------------------------------------------------
 
 constexpr int kFwdThreads = 640;
-constexpr int kW4Stages = 3, kW4Lag = 2, kD4Slots = 4, kW4Rows = 64;
+constexpr int kW4Stages = 3, kW4Lag = 2, kD4Slots = 2, kW4Rows = 64;
 constexpr uint32_t kW4Chunk = 2 * 2 * kW4Rows * kAtomBytes;  // 32 KB: 64 rows x 64 K, hi + lo
 constexpr uint32_t kFwdW4 = kOffW3T;                         // W4 ring after W1, W2, W3
 constexpr uint32_t kStageRow = kW4Rows * 4 + 16;             // padded row of the output staging
 constexpr uint32_t kFwdOut = kFwdW4 + kW4Stages * kW4Chunk;  // gate chunk staging [128][kStageRow]
 constexpr uint32_t kFwdBar = kFwdOut + kTile * kStageRow;
 constexpr uint32_t kFwdSmem = kFwdBar + 256 + 1024;
-constexpr uint32_t kColH = 64, kColHLo = 128, kColF = 192, kColFLo = 200, kColOut = 256;
+constexpr uint32_t kColH0 = 64, kColHStep = 128, kColF = 320, kColFLo = 328, kColOut = 384;
 
 struct FwdBars {
-  uint64_t op_ready, acc_full, h_free;
+  uint64_t op_ready, acc_full, h3_ready[2], h_free[2];
   uint64_t w4_full[kW4Stages], w4_empty[kW4Stages];
   uint64_t d4_full[kD4Slots], d4_empty[kD4Slots];
   uint32_t tmem_slot;
@@ -228,12 +228,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1) radial_forward_kernel(RadialAr
   const uint32_t warp = threadIdx.x / 32;
   const int chunks = a.gates_width / kW4Rows;
   const int64_t tiles = (a.edges + kTile - 1) / kTile;
+  const int64_t my_tiles = tiles > blockIdx.x ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
 
   copy_flat(smem, a.image, kOffW3T);                 // W1, W2, W3
   if (threadIdx.x == 0) {
     mbar_init(&b->op_ready, 1);
     mbar_init(&b->acc_full, 1);
-    mbar_init(&b->h_free, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&b->h3_ready[i], 1);
+      mbar_init(&b->h_free[i], 1);
+    }
     for (int i = 0; i < kW4Stages; ++i) {
       mbar_init(&b->w4_full[i], 1);
       mbar_init(&b->w4_empty[i], 1);
@@ -254,74 +258,88 @@ __global__ void __launch_bounds__(kFwdThreads, 1) radial_forward_kernel(RadialAr
   const unsigned char* w4_image = a.image + kOffW4;
   const uint32_t id64 = idesc_tf32(kTile, kHidden);
 
-  if (warp == 0) {
-    if (threadIdx.x == 0) {
-      // ----- control -----
-      uint32_t op_phase = 0, full_phase[kW4Stages] = {}, empty_phase[kW4Stages] = {}, d4e_phase[kD4Slots] = {};
-      int64_t wcount = 0, issued = 0;                // W4 chunks consumed / requested (CTA lifetime)
-      const int64_t my_tiles = tiles > blockIdx.x ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-      const int64_t total_chunks = my_tiles * chunks;
-      auto request = [&](int64_t n) {                // bulk-load chunk sequence item n into its stage
-        const int st = (int)(n % kW4Stages);
-        mbar_arrive_expect(&b->w4_full[st], kW4Chunk);
-        bulk_load(smem + kFwdW4 + st * kW4Chunk, w4_image + (uint64_t)(n % chunks) * kW4Chunk, kW4Chunk,
-                  &b->w4_full[st]);
-      };
-      for (; issued < total_chunks && issued < kW4Stages - kW4Lag; ++issued) request(issued);
-      bool ok = true;
-      auto wait_op = [&]() {
-        ok = ok && mbar_wait_or_abort(&b->op_ready, op_phase, kWaitNs, abort);
-        op_phase ^= 1u;
-        fence_after_sync();
-        return ok;
-      };
-      for (int64_t i = 0; i < my_tiles && ok; ++i) {
-        if (!wait_op()) break;                       // features in TMEM
-        mma_tf32x3_ta(tmem, tmem + kColF, tmem + kColFLo, base + kOffW1, base + kOffW1 + 32, id64, 0u);
+  if (threadIdx.x == 0) {
+    // ----- hidden issuer -----
+    uint32_t op_phase = 0;
+    bool ok = true;
+    auto wait_op = [&]() {
+      ok = ok && mbar_wait_or_abort(&b->op_ready, op_phase, kWaitNs, abort);
+      op_phase ^= 1u;
+      fence_after_sync();
+      return ok;
+    };
+    for (int64_t i = 0; i < my_tiles && ok; ++i) {
+      const uint32_t h = tmem + kColH0 + kColHStep * (uint32_t)(i & 1);
+      if (!wait_op()) break;                         // features in TMEM
+      mma_tf32x3_ta(tmem, tmem + kColF, tmem + kColFLo, base + kOffW1, base + kOffW1 + 32, id64, 0u);
+      mma_commit(&b->acc_full);
+      for (int layer = 0; layer < 2 && ok; ++layer) {
+        if (!wait_op()) break;                       // h1, h2 in this tile's buffer
+        gemm_k64_ta(tmem, h, h + 64, base + (layer == 0 ? kOffW2 : kOffW3), kHidden, id64);
         mma_commit(&b->acc_full);
-        for (int layer = 0; layer < 2 && ok; ++layer) {
-          if (!wait_op()) break;                     // h1, h2 in TMEM
-          gemm_k64_ta(tmem, tmem + kColH, tmem + kColHLo, base + (layer == 0 ? kOffW2 : kOffW3), kHidden, id64);
-          mma_commit(&b->acc_full);
-        }
-        if (!ok || !wait_op()) break;                // h3 in TMEM
-        for (int j = 0; j < chunks && ok; ++j, ++wcount) {
-          const int st = (int)(wcount % kW4Stages), slot = (int)(wcount % kD4Slots);
-          if (issued < total_chunks) {               // refill the stage read kW4Lag chunks ago
-            const int fs = (int)(issued % kW4Stages);
-            if (issued >= kW4Stages) {
-              ok = mbar_wait_or_abort(&b->w4_empty[fs], empty_phase[fs], kWaitNs, abort);
-              empty_phase[fs] ^= 1u;
-              if (!ok) break;
-            }
-            request(issued++);
-          }
-          ok = mbar_wait_or_abort(&b->w4_full[st], full_phase[st], kWaitNs, abort);
-          full_phase[st] ^= 1u;
-          if (ok && wcount >= kD4Slots) {
-            ok = mbar_wait_or_abort(&b->d4_empty[slot], d4e_phase[slot], kWaitNs, abort);
-            d4e_phase[slot] ^= 1u;
-          }
-          if (!ok) break;
-          fence_after_sync();
-          gemm_k64_ta(tmem + kColOut + kW4Rows * slot, tmem + kColH, tmem + kColHLo, base + kFwdW4 + st * kW4Chunk,
-                      kW4Rows, idesc_tf32(kTile, kW4Rows));
-          mma_commit(&b->d4_full[slot]);
-          mma_commit(&b->w4_empty[st]);
-        }
-        mma_commit(&b->h_free);                      // h3 may be overwritten once these MMAs finish
       }
     }
+    // The hidden group consumes the last acc_full only after that MMA completed.
+  } else if (threadIdx.x == 32) {
+    // ----- output issuer -----
+    uint32_t h3_phase[2] = {}, full_phase[kW4Stages] = {}, empty_phase[kW4Stages] = {}, d4e_phase[kD4Slots] = {};
+    int64_t wcount = 0, issued = 0;
+    const int64_t total_chunks = my_tiles * chunks;
+    auto request = [&](int64_t n) {
+      const int st = (int)(n % kW4Stages);
+      mbar_arrive_expect(&b->w4_full[st], kW4Chunk);
+      bulk_load(smem + kFwdW4 + st * kW4Chunk, w4_image + (uint64_t)(n % chunks) * kW4Chunk, kW4Chunk,
+                &b->w4_full[st]);
+    };
+    for (; issued < total_chunks && issued < kW4Stages - kW4Lag; ++issued) request(issued);
+    bool ok = true;
+    int64_t i = 0;
+    for (; i < my_tiles && ok; ++i) {
+      const uint32_t buf = (uint32_t)(i & 1);
+      const uint32_t h = tmem + kColH0 + kColHStep * buf;
+      ok = mbar_wait_or_abort(&b->h3_ready[buf], h3_phase[buf], kWaitNs, abort);
+      h3_phase[buf] ^= 1u;
+      if (!ok) break;
+      for (int j = 0; j < chunks && ok; ++j, ++wcount) {
+        const int st = (int)(wcount % kW4Stages), slot = (int)(wcount % kD4Slots);
+        if (issued < total_chunks) {                 // refill the stage read kW4Lag chunks ago
+          const int fs = (int)(issued % kW4Stages);
+          if (issued >= kW4Stages) {
+            ok = mbar_wait_or_abort(&b->w4_empty[fs], empty_phase[fs], kWaitNs, abort);
+            empty_phase[fs] ^= 1u;
+            if (!ok) break;
+          }
+          request(issued++);
+        }
+        ok = mbar_wait_or_abort(&b->w4_full[st], full_phase[st], kWaitNs, abort);
+        full_phase[st] ^= 1u;
+        if (ok && wcount >= kD4Slots) {
+          ok = mbar_wait_or_abort(&b->d4_empty[slot], d4e_phase[slot], kWaitNs, abort);
+          d4e_phase[slot] ^= 1u;
+        }
+        if (!ok) break;
+        fence_after_sync();
+        gemm_k64_ta(tmem + kColOut + kW4Rows * slot, h, h + 64, base + kFwdW4 + st * kW4Chunk, kW4Rows,
+                    idesc_tf32(kTile, kW4Rows));
+        mma_commit(&b->d4_full[slot]);
+        mma_commit(&b->w4_empty[st]);
+      }
+      mma_commit(&b->h_free[buf]);                   // this buffer may be overwritten once these finish
+    }
+    // Wait (bounded) for the last commit so every MMA of this issuer is complete.
+    if (i > 0) mbar_wait(&b->h_free[(i - 1) & 1], (uint32_t)(((i - 1) >> 1) & 1), kWaitNs);
   } else if (warp >= 4 && warp < 12) {
     // ----- hidden group: 8 warps, quadrant warp % 4, column half (warp - 4) / 4 -----
     const uint32_t row = (warp % 4) * 32 + threadIdx.x % 32;
     const uint32_t half = (warp - 4) / 4;
     const uint32_t lanes = tmem + (((warp % 4) * 32) << 16);
-    uint32_t acc_phase = 0, hfree_phase = 0;
+    uint32_t acc_phase = 0, hfree_phase[2] = {};
     bool ok = true;
     int64_t count = 0;
     for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++count) {
       const int64_t e = t * kTile + row;
+      const uint32_t buf = (uint32_t)(count & 1);
+      const uint32_t hcol = kColH0 + kColHStep * buf;
       if (half == 0) {
         float f[8], hi[8], lo[8];
 #pragma unroll
@@ -340,9 +358,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) radial_forward_kernel(RadialAr
         ok = named_barrier_all(1, 256, mbar_wait_or_abort(&b->acc_full, acc_phase, kWaitNs, abort));
         acc_phase ^= 1u;
         if (!ok) break;
-        if (layer == 0 && count > 0) {               // the previous tile's W4 MMAs still read h3
-          ok = named_barrier_all(1, 256, mbar_wait_or_abort(&b->h_free, hfree_phase, kWaitNs, abort));
-          hfree_phase ^= 1u;
+        if (layer == 0 && count >= 2) {              // tile count-2's W4 MMAs still read this buffer
+          ok = named_barrier_all(1, 256, mbar_wait_or_abort(&b->h_free[buf], hfree_phase[buf], kWaitNs, abort));
+          hfree_phase[buf] ^= 1u;
           if (!ok) break;
         }
         fence_after_sync();
@@ -357,13 +375,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1) radial_forward_kernel(RadialAr
             hi[i] = tf32_hi(h);
             lo[i] = h - hi[i];
           }
-          tmem_store16_async(lanes + kColH + 32 * half + 16 * q, hi);
-          tmem_store16_async(lanes + kColHLo + 32 * half + 16 * q, lo);
+          tmem_store16_async(lanes + hcol + 32 * half + 16 * q, hi);
+          tmem_store16_async(lanes + hcol + 64 + 32 * half + 16 * q, lo);
         }
         tmem_store_wait();
         fence_before_sync();
         named_barrier(1, 256);
-        if (threadIdx.x == 128) mbar_arrive(&b->op_ready);
+        if (threadIdx.x == 128) mbar_arrive(layer < 2 ? &b->op_ready : &b->h3_ready[buf]);
       }
     }
   } else if (warp >= 12) {
@@ -375,7 +393,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1) radial_forward_kernel(RadialAr
     int64_t wcount = 0;
     bool ok = true;
     for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-      const int64_t e = t * kTile + row;
       for (int j = 0; j < chunks; ++j, ++wcount) {
         const int slot = (int)(wcount % kD4Slots);
         // Group-wide: all reads of the previous chunk's staging are done, and all agree on ok.
@@ -406,15 +423,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) radial_forward_kernel(RadialAr
       }
     }
   }
-  // Teardown: the control thread's last commit (h_free) covers every MMA it issued.
   __syncthreads();
   if (threadIdx.x == 0 && *abort) flag_error(a.status, 4);
   if (warp == 0) {
-    const int64_t my_tiles = tiles > blockIdx.x ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-    if (my_tiles > 0 && threadIdx.x == 0) {
-      // h_free completes once per tile; the last completion has parity (my_tiles - 1) & 1.
-      mbar_wait(&b->h_free, (uint32_t)((my_tiles - 1) & 1), kWaitNs);
-    }
     __syncwarp();
     fence_after_sync();
     tmem_dealloc(tmem, 512);
