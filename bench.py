@@ -58,6 +58,9 @@ def parse_args():
     p.add_argument("--profile-md", action="store_true",
                    help="time only the configs[4] MD step (torchrun for several GPUs)")
     p.add_argument("--profile-train", action="store_true", help="time only the configs[3] training step")
+    p.add_argument("--profile-radial", action="store_true",
+                   help="time only the fused radial MLP kernels (forward, backward) at --rows edges, --gates columns")
+    p.add_argument("--gates", type=int, default=704, help="gate columns of --profile-radial (11 paths x C64)")
     return p.parse_args()
 
 
@@ -621,6 +624,30 @@ def run_profile(args):
                       "vjp_ms": round(vjp_ms, 4), "vjp_GBps": round(VJP_BYTES * rows_v / vjp_ms / 1e6, 1)}))
 
 
+def run_profile_radial(args):
+    """Fused radial MLP alone: seeded weights (8 -> 64 -> 64 -> 64 -> G) and edge embeddings,
+    forward and embedding-gradient kernels timed with CUDA events (for ncu command lines)."""
+    device = torch.device("cuda", 0)
+    from ictc_o3.backends.cuda import radial
+    rows = args.rows or 1048576
+    g = torch.Generator().manual_seed(11)
+    weights = [torch.randn(64, 8, generator=g) / 8 ** 0.5, torch.randn(64, 64, generator=g) / 8.0,
+               torch.randn(64, 64, generator=g) / 8.0, torch.randn(args.gates, 64, generator=g) / 8.0]
+    plan = radial.RadialPlan()
+    image, status = plan.get([w.to(device) for w in weights])
+    feats = torch.rand(rows, 8, device=device)
+    grad = torch.randn(rows, args.gates, device=device)
+    fwd_ms = time_loop(lambda: radial._forward(image, status, feats, args.gates), args.steps, args.warmup, 1,
+                       device) / args.steps
+    bwd_ms = time_loop(lambda: radial._backward(image, status, feats, grad), args.steps, args.warmup, 1,
+                       device) / args.steps
+    radial.check_status(plan)
+    gate_bytes = rows * args.gates * 4
+    print(json.dumps({"profile_radial": True, "rows": rows, "gates": args.gates, "fwd_ms": round(fwd_ms, 4),
+                      "fwd_GBps_gates": round(gate_bytes / fwd_ms / 1e6, 1), "bwd_ms": round(bwd_ms, 4),
+                      "bwd_GBps_gates": round(gate_bytes / bwd_ms / 1e6, 1)}), flush=True)
+
+
 def main():
     args = parse_args()
     if args.profile_block:
@@ -628,6 +655,8 @@ def main():
         from ictc_o3.backends.cuda import _native
         _native.library()
         print(json.dumps({"profile_block": mace_block(device, args.steps, args.warmup, atoms=args.atoms or 16384)}))
+    elif args.profile_radial:
+        run_profile_radial(args)
     elif args.profile_train:
         device = torch.device("cuda", 0)
         from ictc_o3.backends.cuda import _native

@@ -144,6 +144,27 @@ def _monomial_factors(dim: int, correlation: int, device):
             for a in range(correlation)], len(rows)
 
 
+_SELECTIONS = {}
+
+
+def _selection_matrices(dim: int, correlation: int, device, dtype):
+    """One-hot [dim + 1, rows] matrices: column r of matrix a picks the a-th factor of
+    monomial r (index dim = the constant 1).  Gathering factors as matrix products
+    keeps every derivative of the polynomial a GEMM (an indexed gather would
+    differentiate into a sort-based scatter)."""
+    key = (dim, correlation, str(device), dtype)
+    mats = _SELECTIONS.get(key)
+    if mats is None:
+        factors, rows = _monomial_factors(dim, correlation, device)
+        mats = []
+        for idx in factors:
+            m = torch.zeros(dim + 1, rows, device=device, dtype=dtype)
+            m[idx, torch.arange(rows, device=device)] = 1.0
+            mats.append(m)
+        _SELECTIONS[key] = mats
+    return mats
+
+
 def polynomial(x, table, tiles, tile_species, spec):
     """The contraction as differentiable device tensor algebra (second-order path).
 
@@ -158,16 +179,17 @@ def polynomial(x, table, tiles, tile_species, spec):
     feats = torch.cat([x[:, l * l * channels:(l + 1) ** 2 * channels].reshape(n, channels, 2 * l + 1)
                        for l in range(lmax + 1)], -1)
     f1 = torch.cat([feats, torch.ones_like(feats[:, :, :1])], -1)
-    factors, rows = _monomial_factors(dim, correlation, x.device)
+    select = _selection_matrices(dim, correlation, x.device, x.dtype)
+    rows = select[0].shape[1]
     species = tile_species.to(torch.int64)
     blocks = [x.new_zeros(n, channels, 2 * t + 1) for t in range(target_lmax + 1)]
     for s in torch.unique(species).tolist():
         nodes = tiles[species == s].reshape(-1)
         nodes = nodes[nodes >= 0]
         f = f1.index_select(0, nodes)
-        mono = f[:, :, factors[0]]
+        mono = torch.matmul(f, select[0])
         for a in range(1, correlation):
-            mono = mono * f[:, :, factors[a]]                         # [n_s, C, R]
+            mono = mono * torch.matmul(f, select[a])                  # [n_s, C, R]
         offset = 0
         for t in range(target_lmax + 1):
             M = 2 * t + 1
