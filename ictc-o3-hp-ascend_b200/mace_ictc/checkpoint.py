@@ -1,0 +1,164 @@
+"""State-dict compatibility with the reference ``PureCartesianICTDFix`` checkpoints.
+
+Maps the parameter names of the reference model
+(``mace_ictc/models/pure_cartesian_ictd_fix.py:2058-2765``) onto ``MACEICTC`` for
+the configuration this backend implements (residual interaction blocks with the
+path-preserving TP, pure-ICTC symmetric contraction product blocks, linear layer
+readouts and the MLP last readout):
+
+==============================================================  =====================================
+reference key                                                   this model
+==============================================================  =====================================
+node_embedding.weight                                           node_embedding.weight
+interactions.i.linear_up.adapters.l.weight      (:1519)         interactions.i.linear_up.weights.l
+interactions.i.tp.weight                        (:1520)         interactions.i.tp.weight
+interactions.i.fc.{0,2,4,6}.weight              (:1545-1553)    interactions.i.fc.{0,2,4,6}.weight
+interactions.i.message_linear.weights.l         (:629-661)      interactions.i.message_linear.weights.l
+interactions.i.self_connection.weights.l        (:335-392)      interactions.i.self_connection.weight[:, l]
+interactions.i.message_selector.weights.l                       interactions.i.message_selector.weight[:, l]
+products.i.symmetric_contractions.contractions.t.*  (:1202-1395) same names (weights_max, weights.j, U_matrix_nu)
+products.i.linear.weight  (e3nn o3.Linear, :1419)               products.i.linear.weights.l
+layer_energy_readouts.i.readout.weight                          layer_readouts.i.weight
+last_layer_energy_readout.linear_{1,2}.weight   (:1434-1449)    last_readout.{0,2}.weight
+==============================================================  =====================================
+
+The product linear is e3nn's ``o3.Linear`` on ``C x (0e + 1o + 2e + ...)``: its flat
+weight holds one ``[mul_in, mul_out]`` block per degree, applied with the
+``1/sqrt(mul_in)`` path normalisation, so ``W_l[out, in] = w_l[in, out] / sqrt(C)``.
+Optional reference features this model does not implement (normalisations,
+per-degree output scales, biases, attention, energy scale/shift, head scales) are
+accepted only at their identity values; anything else raises.
+"""
+from __future__ import annotations
+
+import math
+import re
+from typing import Dict, List
+
+import torch
+
+
+# Reference keys of optional features, with the check that makes them an identity.
+def _identity(key: str, value: torch.Tensor) -> bool:
+    if key.endswith("log_scale"):
+        return bool(torch.all(value == 0))
+    if re.search(r"\.bias(\.|$)", key):
+        return bool(torch.all(value == 0))
+    if key.endswith("readout_head_scales"):
+        return bool(torch.all(value == 1))
+    if key.endswith("energy_output_scale"):
+        return value is None or bool(torch.all(value == 1))
+    if key.endswith("energy_output_shift"):
+        return value is None or bool(torch.all(value == 0))
+    return False
+
+
+def _e3nn_linear_to_blocks(flat: torch.Tensor, channels: int, lmax: int) -> List[torch.Tensor]:
+    block = channels * channels
+    if flat.numel() != block * (lmax + 1):
+        raise ValueError(f"product linear weight has {flat.numel()} values, expected {block * (lmax + 1)}")
+    return [flat[l * block:(l + 1) * block].reshape(channels, channels).t() / math.sqrt(channels)
+            for l in range(lmax + 1)]
+
+
+def _blocks_to_e3nn_linear(weights, channels: int) -> torch.Tensor:
+    return torch.cat([(w.t() * math.sqrt(channels)).reshape(-1) for w in weights])
+
+
+def from_reference_state_dict(model, state: Dict[str, torch.Tensor], strict: bool = True) -> List[str]:
+    """Load a reference checkpoint's state dict into ``model`` (a ``MACEICTC``).
+
+    Returns the reference keys accepted as identities.  With ``strict``, unknown
+    keys and missing parameters raise."""
+    own = dict(model.named_parameters())
+    own.update(dict(model.named_buffers()))
+    target: Dict[str, torch.Tensor] = {}
+    accepted: List[str] = []
+    unknown: List[str] = []
+    element_blocks: Dict[str, Dict[int, torch.Tensor]] = {}
+    for key, value in state.items():
+        if value is None:
+            continue
+        m = re.fullmatch(r"interactions\.(\d+)\.linear_up\.adapters\.(\d+)\.weight", key)
+        if m:
+            target[f"interactions.{m[1]}.linear_up.weights.{m[2]}"] = value
+            continue
+        m = re.fullmatch(r"interactions\.(\d+)\.(tp\.weight|fc\.\d+\.weight|message_linear\.weights\.\d+)", key)
+        if m:
+            target[key] = value
+            continue
+        m = re.fullmatch(r"interactions\.(\d+)\.(self_connection|message_selector)\.weights\.(\d+)", key)
+        if m:
+            element_blocks.setdefault(f"interactions.{m[1]}.{m[2]}.weight", {})[int(m[3])] = value
+            continue
+        if key.startswith("products.") and ".symmetric_contractions.contractions." in key:
+            target[key] = value
+            continue
+        m = re.fullmatch(r"products\.(\d+)\.linear\.weight", key)
+        if m:
+            lin = model.products[int(m[1])].linear
+            for l, w in enumerate(_e3nn_linear_to_blocks(value, lin.out_channels, lin.lmax)):
+                target[f"products.{m[1]}.linear.weights.{l}"] = w
+            continue
+        m = re.fullmatch(r"layer_energy_readouts\.(\d+)\.readout\.weight", key)
+        if m:
+            target[f"layer_readouts.{m[1]}.weight"] = value
+            continue
+        m = re.fullmatch(r"last_layer_energy_readout\.linear_([12])\.weight", key)
+        if m:
+            target[f"last_readout.{0 if m[1] == '1' else 2}.weight"] = value
+            continue
+        if key == "node_embedding.weight":
+            target[key] = value
+            continue
+        if _identity(key, value):
+            accepted.append(key)
+            continue
+        unknown.append(key)
+    for name, blocks in element_blocks.items():
+        target[name] = torch.stack([blocks[l] for l in sorted(blocks)], 1)
+    if strict and unknown:
+        raise NotImplementedError(f"reference keys without a counterpart in this model: {unknown}")
+    with torch.no_grad():
+        for name, value in target.items():
+            if name not in own:
+                if strict:
+                    raise KeyError(f"{name} (mapped from the reference checkpoint) is not a parameter of this model")
+                continue
+            if own[name].shape != value.shape:
+                raise ValueError(f"{name}: shape {tuple(value.shape)} does not match {tuple(own[name].shape)}")
+            own[name].copy_(value)
+    if strict:
+        missing = [n for n, p in model.named_parameters() if n not in target]
+        if missing:
+            raise KeyError(f"parameters not set by the reference checkpoint: {missing}")
+    return accepted
+
+
+def to_reference_state_dict(model) -> Dict[str, torch.Tensor]:
+    """The inverse mapping: a state dict with the reference's names and layouts."""
+    out: Dict[str, torch.Tensor] = {"node_embedding.weight": model.node_embedding.weight.detach().clone()}
+    for i, block in enumerate(model.interactions):
+        p = f"interactions.{i}"
+        for l, w in enumerate(block.linear_up.weights):
+            out[f"{p}.linear_up.adapters.{l}.weight"] = w.detach().clone()
+        out[f"{p}.tp.weight"] = block.tp.weight.detach().clone()
+        for idx, m in enumerate(block.fc):
+            if isinstance(m, torch.nn.Linear):
+                out[f"{p}.fc.{idx}.weight"] = m.weight.detach().clone()
+        for l, w in enumerate(block.message_linear.weights):
+            out[f"{p}.message_linear.weights.{l}"] = w.detach().clone()
+        for name in ("self_connection", "message_selector"):
+            mod = getattr(block, name)
+            if mod is not None:
+                for l in range(mod.lmax + 1):
+                    out[f"{p}.{name}.weights.{l}"] = mod.weight[:, l].detach().clone()
+    for i, prod in enumerate(model.products):
+        for k, v in prod.symmetric_contractions.state_dict().items():
+            out[f"products.{i}.symmetric_contractions.{k}"] = v.detach().clone()
+        out[f"products.{i}.linear.weight"] = _blocks_to_e3nn_linear(list(prod.linear.weights), prod.linear.out_channels)
+    for i, r in enumerate(model.layer_readouts):
+        out[f"layer_energy_readouts.{i}.readout.weight"] = r.weight.detach().clone()
+    out["last_layer_energy_readout.linear_1.weight"] = model.last_readout[0].weight.detach().clone()
+    out["last_layer_energy_readout.linear_2.weight"] = model.last_readout[2].weight.detach().clone()
+    return out

@@ -1,0 +1,71 @@
+"""Reference state-dict names and layouts load into the model (CPU, FP64 oracle ops)."""
+import math
+
+import pytest
+import torch
+
+
+def _model(seed):
+    from mace_ictc.models import MACEICTC
+    from oracle.model_ops import OracleOps
+    torch.manual_seed(seed)
+    return MACEICTC(channels=8, lmax=2, r_max=3.0, avg_num_neighbors=5.0, ops=OracleOps()).double()
+
+
+def _system():
+    gen = torch.Generator().manual_seed(1)
+    side = 8.0
+    pos = torch.rand(30, 3, generator=gen, dtype=torch.float64) * side
+    species = torch.randint(0, 3, (30,), generator=gen)
+    d = pos[:, None, :] - pos[None, :, :]
+    shift = -side * torch.round(d / side)
+    dist = (d + shift).norm(dim=-1)
+    i, j = torch.nonzero((dist < 3.0) & (dist > 0), as_tuple=True)
+    return pos, species, j, i, shift[i, j]
+
+
+def test_reference_names_round_trip():
+    from mace_ictc.checkpoint import from_reference_state_dict, to_reference_state_dict
+    source, target = _model(1), _model(2)
+    ref = to_reference_state_dict(source)
+    assert "interactions.0.linear_up.adapters.0.weight" in ref
+    assert "products.0.linear.weight" in ref and ref["products.0.linear.weight"].dim() == 1
+    from_reference_state_dict(target, ref)
+    for (n, a), (m, b) in zip(source.named_parameters(), target.named_parameters()):
+        assert n == m and torch.allclose(a, b, rtol=1e-15, atol=1e-15), n   # e3nn scaling round trip
+    pos, species, src, dst, shift = _system()
+    assert torch.allclose(source.energy(pos, species, src, dst, shift), target.energy(pos, species, src, dst, shift),
+                          rtol=1e-12, atol=1e-12)
+
+
+def test_e3nn_linear_convention():
+    """The product linear follows e3nn's o3.Linear: [mul_in, mul_out] blocks / sqrt(mul_in)."""
+    from mace_ictc.checkpoint import from_reference_state_dict, to_reference_state_dict
+    model = _model(3)
+    ref = to_reference_state_dict(model)
+    C = model.channels
+    flat = torch.randn(C * C * (model.products[0].linear.lmax + 1), dtype=torch.float64)
+    ref["products.0.linear.weight"] = flat
+    from_reference_state_dict(model, ref)
+    x = torch.randn(5, C, dtype=torch.float64)
+    w0 = flat[:C * C].reshape(C, C)                                   # [in, out]
+    want = x @ w0 / math.sqrt(C)                                      # e3nn: sum_i x_i w[i, o] / sqrt(C)
+    got = x @ model.products[0].linear.weights[0].t()
+    assert torch.allclose(got, want)
+
+
+def test_identity_options_accepted_others_rejected():
+    from mace_ictc.checkpoint import from_reference_state_dict, to_reference_state_dict
+    model = _model(4)
+    ref = to_reference_state_dict(model)
+    ref["interactions.0.message_output_scale.log_scale"] = torch.zeros(3, 8, dtype=torch.float64)
+    ref["readout_head_scales"] = torch.ones(2, dtype=torch.float64)
+    accepted = from_reference_state_dict(model, ref)
+    assert "readout_head_scales" in accepted
+    ref["interactions.0.message_output_scale.log_scale"] = torch.full((3, 8), 0.1, dtype=torch.float64)
+    with pytest.raises(NotImplementedError):
+        from_reference_state_dict(model, ref)
+    ref = to_reference_state_dict(model)
+    ref["interactions.0.attn_q_proj.weight"] = torch.zeros(8, 8, dtype=torch.float64)
+    with pytest.raises(NotImplementedError):
+        from_reference_state_dict(model, ref)
