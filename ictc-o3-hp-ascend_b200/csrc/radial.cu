@@ -450,31 +450,11 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-__device__ __forceinline__ void issue_chunk(const RadialArgs& a, uint32_t stage, int64_t tile, int chunk) {
-  // A: rows of dgates, 32 values (8 x 16 B) per row, swizzled into the A-hi buffer.
-#pragma unroll
-  for (int i = 0; i < 1024 / kThreads; ++i) {
-    const uint32_t idx = threadIdx.x + kThreads * i;
-    const uint32_t r = idx / 8, ch = idx % 8;
-    const int64_t e = tile * kTile + r;
-    const bool valid = e < a.edges;
-    const float* src = valid ? a.grad_gates + e * a.gates_width + chunk * 32 + ch * 4 : a.grad_gates;
-    cp_async16(stage + sw128_chunk(r, ch), src, valid ? 16u : 0u);
-  }
-  // B: the chunk's W4^T image (hi 8 KB, lo 8 KB), flat.
-  const unsigned char* img = a.image + kOffW4 + (uint64_t)a.gates_width * 512u + (uint64_t)chunk * 16384u;
-#pragma unroll
-  for (int i = 0; i < 1024 / kThreads; ++i) {
-    const uint32_t idx = threadIdx.x + kThreads * i;
-    cp_async16(stage + 2 * 16384 + idx * 16, img + idx * 16, 16u);
-  }
-}
-
-// Warp-specialised: warp 0 lane 0 issues the MMAs; warps 4..19 (the workers) load
-// dgates rows and W4^T chunks with cp.async, split dgates into hi/lo in place, and
-// write dh3.  Two sets of kAccumulators TMEM accumulators alternate between tiles
+// Warp-specialised: warp 0 lane 0 issues the MMAs; warps 4..19 (the workers, two
+// groups taking alternate K chunks) load dgates rows and W4^T chunks with
+// cp.async, split dgates into hi/lo in place, and write dh3.  Two sets of kAccumulators TMEM accumulators alternate between tiles
 // so a tile's MMAs can start while the previous tile's dh3 is written.
-constexpr int kAdjThreads = 640, kWorkers = 512;
+constexpr int kAdjThreads = 640;
 
 struct AdjBars {
   uint64_t split_done[kStages], mma_done[kStages], acc_full[2], acc_free[2];
@@ -541,10 +521,14 @@ __global__ void __launch_bounds__(kAdjThreads, 1) radial_w4_adjoint_kernel(Radia
       }
     }
   } else if (warp >= 4) {
-    // ----- workers: 16 warps; epilogue slot = quadrant warp % 4, 16-column slice (warp - 4) / 4 -----
-    const uint32_t wt = threadIdx.x - 128;           // 0 .. 511
+    // ----- workers: two groups of 8 warps; group g handles items q = g, g + 2, ... in
+    // stages g, g + 2 (q % 4), one item ahead.  Epilogue slot: quadrant warp % 4,
+    // 32-column half ((warp - 4) / 4) % 2. -----
+    const uint32_t grp = (warp - 4) / 8;
+    const uint32_t gt = threadIdx.x - 128 - 256 * grp;   // 0 .. 255 within the group
+    const uint32_t bar_id = 1 + grp;
     const uint32_t row = (warp % 4) * 32 + threadIdx.x % 32;
-    const uint32_t slice = (warp - 4) / 4;
+    const uint32_t half = ((warp - 4) / 4) % 2;
     const uint32_t lanes = tmem + (((warp % 4) * 32) << 16);
     uint32_t done_phase[kStages] = {}, full_phase[2] = {};
     bool ok = true;
@@ -553,8 +537,8 @@ __global__ void __launch_bounds__(kAdjThreads, 1) radial_w4_adjoint_kernel(Radia
       const int64_t tile = item_tile(q);
       const int chunk = (int)(q % chunks);
 #pragma unroll
-      for (int i = 0; i < 1024 / kWorkers; ++i) {
-        const uint32_t idx = wt + kWorkers * i;
+      for (int i = 0; i < 1024 / 256; ++i) {
+        const uint32_t idx = gt + 256 * i;
         const uint32_t r = idx / 8, ch = idx % 8;
         const int64_t e = tile * kTile + r;
         const bool valid = e < a.edges;
@@ -563,67 +547,67 @@ __global__ void __launch_bounds__(kAdjThreads, 1) radial_w4_adjoint_kernel(Radia
       }
       const unsigned char* img = a.image + kOffW4 + (uint64_t)a.gates_width * 512u + (uint64_t)chunk * 16384u;
 #pragma unroll
-      for (int i = 0; i < 1024 / kWorkers; ++i) {
-        const uint32_t idx = wt + kWorkers * i;
+      for (int i = 0; i < 1024 / 256; ++i) {
+        const uint32_t idx = gt + 256 * i;
         cp_async16(stage + 2 * 16384 + idx * 16, img + idx * 16, 16u);
       }
     };
-    for (int64_t q = 0; q < kStages - 2; ++q) {
-      if (q < total) issue(q);
-      cp_async_commit();
-    }
-    for (int64_t q = 0; q < total && ok; ++q) {
+    if ((int64_t)grp < total) issue(grp);
+    cp_async_commit();
+    for (int64_t q = grp; q < total && ok; q += 2) {
       const int s = (int)(q % kStages), chunk = (int)(q % chunks);
-      const int64_t next = q + kStages - 2;          // reuses the stage of item q - 2
+      const int64_t next = q + 2;                    // same group, the other stage of the group
       if (next < total) {
-        if (q >= 2) {
+        if (next >= kStages) {                       // that stage last held item next - 4
           const int ns = (int)(next % kStages);
-          ok = named_barrier_all(1, kWorkers, mbar_wait_or_abort(&b->mma_done[ns], done_phase[ns], kWaitNs, abort));
+          ok = named_barrier_all(bar_id, 256, mbar_wait_or_abort(&b->mma_done[ns], done_phase[ns], kWaitNs, abort));
           done_phase[ns] ^= 1u;
           if (!ok) break;
         }
         issue(next);
       }
       cp_async_commit();
-      cp_async_wait<kStages - 2>();
-      named_barrier(1, kWorkers);
+      cp_async_wait<1>();
+      named_barrier(bar_id, 256);
       unsigned char* st = smem + s * kStageBytes;
 #pragma unroll
-      for (int i = 0; i < 1024 / kWorkers; ++i) {
-        const uint32_t off = (wt + kWorkers * i) * 16;
+      for (int i = 0; i < 1024 / 256; ++i) {
+        const uint32_t off = (gt + 256 * i) * 16;
         float4 v = *reinterpret_cast<float4*>(st + off);
         float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
         *reinterpret_cast<float4*>(st + off) = h;
         *reinterpret_cast<float4*>(st + 16384 + off) = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
       }
       fence_async_smem();
-      named_barrier(1, kWorkers);
-      if (wt == 0) mbar_arrive(&b->split_done[s]);
+      named_barrier(bar_id, 256);
+      if (gt == 0) mbar_arrive(&b->split_done[s]);
       if (chunk == chunks - 1) {
         const int64_t ti = q / chunks;
         const uint32_t buf = (uint32_t)(ti & 1);
-        ok = named_barrier_all(1, kWorkers, mbar_wait_or_abort(&b->acc_full[buf], full_phase[buf], kWaitNs, abort));
+        ok = named_barrier_all(bar_id, 256,
+                               mbar_wait_or_abort(&b->acc_full[buf], full_phase[buf], kWaitNs, abort));
         full_phase[buf] ^= 1u;
         if (!ok) break;
         fence_after_sync();
         const int64_t e = item_tile(q) * kTile + row;
-        float v[16];
-        tmem_load16(lanes + 256 * buf + 16 * slice, v);
-        for (int j = 1; j < used; ++j) {
-          float w[16];
-          tmem_load16(lanes + 256 * buf + 64 * j + 16 * slice, w);
+        float v[32];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] += w[i];
+        for (int c = 0; c < 2; ++c) {
+          tmem_load16(lanes + 256 * buf + 32 * half + 16 * c, v + 16 * c);
+          for (int j = 1; j < used; ++j) {
+            float w[16];
+            tmem_load16(lanes + 256 * buf + 64 * j + 32 * half + 16 * c, w);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[16 * c + i] += w[i];
+          }
         }
         fence_before_sync();
-        named_barrier(1, kWorkers);
-        if (wt == 0) mbar_arrive(&b->acc_free[buf]);
+        named_barrier(bar_id, 256);
+        if (gt == 0) mbar_arrive(&b->acc_free[buf]);
         if (e < a.edges) {
-          float4* dst = reinterpret_cast<float4*>(a.out_h3 + e * kHidden + 16 * slice);
-          dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-          dst[1] = make_float4(v[4], v[5], v[6], v[7]);
-          dst[2] = make_float4(v[8], v[9], v[10], v[11]);
-          dst[3] = make_float4(v[12], v[13], v[14], v[15]);
+          float4* dst = reinterpret_cast<float4*>(a.out_h3 + e * kHidden + 32 * half);
+#pragma unroll
+          for (int q4 = 0; q4 < 8; ++q4) dst[q4] = make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
         }
       }
     }
