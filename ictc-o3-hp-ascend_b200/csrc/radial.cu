@@ -926,3 +926,44 @@ extern "C" int ictc_radial_backward(const void* image, const float* feats, const
   }
   return ICTC_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Self-test of the bounded waits (failure detection without a GPU fault)
+// ---------------------------------------------------------------------------
+
+namespace ictc {
+namespace {
+
+// One CTA waits on an mbarrier that nothing ever arrives on: the wait must give
+// up after `limit_ns`, record the failure in *status and return normally, leaving
+// the context usable.  `arrive` = 1 makes one thread arrive first (the success path).
+__global__ void wait_selftest_kernel(int* status, uint64_t limit_ns, int arrive) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar, 1);
+    abort_flag = 0;
+  }
+  __syncthreads();
+  if (arrive && threadIdx.x == 0) tc::mbar_arrive(&bar);
+  const bool ok = tc::mbar_wait_or_abort(&bar, 0, limit_ns, &abort_flag);
+  const bool all = __syncthreads_and(ok) != 0;
+  if (threadIdx.x == 0) *status = all ? 0 : 1;
+}
+
+}  // namespace
+}  // namespace ictc
+
+extern "C" int ictc_wait_selftest(int* status, int64_t limit_ns, int arrive, void* stream) {
+  if (!status || limit_ns <= 0 || limit_ns > 5000000000ll) {
+    ictc_set_error("ictc_wait_selftest: invalid argument%s", "");
+    return ICTC_ERR_INVALID;
+  }
+  ictc::wait_selftest_kernel<<<1, 64, 0, (cudaStream_t)stream>>>(status, (uint64_t)limit_ns, arrive);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) {
+    ictc_set_error("ictc_wait_selftest: %s", cudaGetErrorString(err));
+    return ICTC_ERR_CUDA;
+  }
+  return ICTC_OK;
+}

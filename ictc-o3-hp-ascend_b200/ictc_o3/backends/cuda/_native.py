@@ -46,6 +46,7 @@ _SIGNATURES = {
     "ictc_channel_mix": [_p, _i64, _i64, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i, _i, _i, ctypes.c_float, _i,
                          _p],
     "ictc_radial_image_bytes": [_i, _i, _i],
+    "ictc_wait_selftest": [_p, _i64, _i, _p],
     "ictc_radial_pack": [_p, _p, _p, _p, _i, _i, _i, _p, _i64],
     "ictc_radial_forward": [_p, _p, _p, _i64, _i, _i, _i, _p, _p],
     "ictc_radial_backward": [_p, _p, _p, _p, _p, _i64, _i, _i, _i, _p, _p],

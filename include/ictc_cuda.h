@@ -252,6 +252,15 @@ int ictc_channel_mix(const float* x, int64_t x_stride, int64_t x_offset, const f
                      int64_t nodes, int cin, int cout, int degree, float scale, int accumulate, void* stream);
 
 /*
+ * Self-test of the bounded waits used by the tensor-core kernels (no counterpart
+ * in the reference).  One CTA waits on a shared-memory barrier; with arrive = 0
+ * nothing arrives, so the wait must give up after limit_ns (<= 5 s) and the kernel
+ * writes *status = 1 (device int) and returns; with arrive = 1 it writes 0.  The
+ * CUDA context stays usable either way: this is how a lost handoff is reported.
+ */
+int ictc_wait_selftest(int* status, int64_t limit_ns, int arrive, void* stream);
+
+/*
  * Allocation-free neighbour search.  No counterpart in the reference: it exists
  * for callers that cannot allocate device memory during a step (an MD engine
  * that owns all device buffers in its own pool, or a host program using this C
