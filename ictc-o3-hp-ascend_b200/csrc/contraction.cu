@@ -26,9 +26,12 @@ void ictc_set_error(const char* fmt, const char* detail);
 
 namespace ictc {
 
-constexpr int kScNodes = 4;  // nodes per tile (NB)
-// Warps per CTA: the staged inputs (and gradients) take NB * D * 32 floats per warp.
-__host__ __device__ constexpr int sc_warps(int D) { return D > 9 ? 2 : 4; }
+// Nodes per tile (NB): every coefficient row streamed from L2 serves NB nodes, so the
+// table traffic per node falls as 1/NB (the kernels are bound by that stream).
+constexpr int kScNodes = 8;
+// Warps per CTA: the staged inputs (and gradients) take NB * D * 32 floats per warp;
+// static shared memory stays under 48 KB.
+__host__ __device__ constexpr int sc_warps(int D) { return D > 9 ? 1 : 2; }
 
 struct SCArgs {
   const float* __restrict__ x;          // [N, C*D] mul_ir flat
