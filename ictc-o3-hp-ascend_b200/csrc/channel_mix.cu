@@ -45,7 +45,7 @@ struct MixArgs {
 };
 
 template <int M>
-__global__ void __launch_bounds__(256) channel_mix_kernel(MixArgs a) {
+__global__ void __launch_bounds__(256, (M <= 5) ? 2 : 1) channel_mix_kernel(MixArgs a) {
   extern __shared__ __align__(16) float smem[];
   constexpr int kXStride = kChunk * M + 1;        // odd: the 32 node rows hit distinct banks
   float* s_w = smem;                               // [kChunk][kWStride]: s_w[i][o] = W[o0 + o, i0 + i]
