@@ -156,4 +156,15 @@ __device__ __forceinline__ void prefetch_l1(const void* p) {
   asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
 }
 
+// Ask the bulk-copy unit to pull `bytes` at p into L2 (p 16-byte aligned, bytes a
+// multiple of 16); one instruction per row, issued by the lane that owns the row.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Rows of `bytes` starting at base + r * bytes can be bulk-prefetched.
+__device__ __forceinline__ bool bulk_rows(const void* base, uint32_t bytes) {
+  return base != nullptr && ((reinterpret_cast<uintptr_t>(base) | bytes) & 15u) == 0;
+}
+
 }  // namespace ictc

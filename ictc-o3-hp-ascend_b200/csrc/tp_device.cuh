@@ -47,6 +47,9 @@ struct CoefParams {
 };
 
 constexpr int kWarps = 8;
+// Graph kernels: how many edges ahead of the one being computed the gathered
+// and streamed rows are pulled into L2.
+constexpr int kAheadL2 = 4;
 constexpr int kThreads = kWarps * 32;
 
 __host__ __device__ constexpr int round4(int n) { return (n + 3) & ~3; }

@@ -16,6 +16,70 @@
 
 namespace ictc {
 
+// bond_e[p, i, k] is identically zero when no harmonic component j couples (i, k)
+// (28% of the (i, k) pairs up to l = 3); such entries are never formed.
+template <int L1, int L2, int L3, int I, int K>
+struct BondNonzero {
+  static constexpr bool value = [] {
+    for (int j = 0; j < 2 * L2 + 1; ++j)
+      if (cg_nonzero(L1, L2, L3, I, j, K)) return true;
+    return false;
+  }();
+};
+
+// One bond entry of the message and adjoint kernels, formed in registers:
+// sum_j C_p[i,j,k] Y_{l2}[j] over the structurally non-zero j, with the CG values
+// read at compile-time offsets from the kernel's parameter bank (FFMA constant
+// operands) and y = the edge's degree-l2 harmonics.
+template <int L1, int L2, int L3, int CO, int I, int K, int CT>
+__device__ __forceinline__ float bond_entry(const float (&coef)[CT], const float (&y)[2 * L2 + 1]) {
+  constexpr int m2 = 2 * L2 + 1, m3 = 2 * L3 + 1;
+  float b = 0.f;
+  static_for<m2>([&](auto jc) {
+    constexpr int j = decltype(jc)::value;
+    if constexpr (CgNonzero<L1, L2, L3, I, j, K>::value) b = fmaf(coef[CO + (I * m3 + K) * m2 + j], y[j], b);
+  });
+  return b;
+}
+
+template <int L2>
+__device__ __forceinline__ void load_harmonics(float (&y)[2 * L2 + 1], const float* s_y) {
+#pragma unroll
+  for (int j = 0; j < 2 * L2 + 1; ++j) y[j] = s_y[L2 * L2 + j];
+}
+
+// Column sums over a warp.  P = N rounded up to a power of two, S = log2(32 / P).
+// On return lane L holds the total over the 32 lanes of column L >> S.  Each
+// halving step keeps half of the live columns and trades the other half with the
+// partner lane, so the N columns cost P - 1 + S shuffles instead of 5 N.
+template <int N>
+struct ColumnSum {
+  static constexpr int P = N <= 1 ? 1 : N <= 2 ? 2 : N <= 4 ? 4 : N <= 8 ? 8 : N <= 16 ? 16 : 32;
+  static constexpr int S = P == 1 ? 5 : P == 2 ? 4 : P == 4 ? 3 : P == 8 ? 2 : P == 16 ? 1 : 0;
+};
+
+template <int N>
+__device__ __forceinline__ float warp_column_sum(const float (&v)[N], int lane) {
+  static_assert(N <= 32, "at most 32 columns");
+  constexpr int P = ColumnSum<N>::P;
+  float w[P];
+#pragma unroll
+  for (int q = 0; q < P; ++q) w[q] = q < N ? v[q] : 0.f;
+#pragma unroll
+  for (int half = P / 2, off = 16; half >= 1; half >>= 1, off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int q = 0; q < half; ++q) {
+      const float keep = upper ? w[q + half] : w[q];
+      const float send = upper ? w[q] : w[q + half];
+      w[q] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+#pragma unroll
+  for (int off = (32 / P) >> 1; off > 0; off >>= 1) w[0] += __shfl_xor_sync(0xffffffffu, w[0], off);
+  return w[0];
+}
+
 // ---------------------------------------------------------------------------
 // Standalone forward: one warp per (instance, channel slice); every output
 // block is written straight from registers with streaming stores.
@@ -107,19 +171,17 @@ __global__ void __launch_bounds__(kThreads) tp_forward_kernel(TPArgs a) {
 // arrive in lane-parallel batches of 32.
 // ---------------------------------------------------------------------------
 template <int LI, int LE, int LO, int CPL, int LAYOUT>
-__global__ void __launch_bounds__(kThreads, (LO >= 3) ? 1 : 2) tp_message_forward_kernel(TPArgs a) {
+__global__ void __launch_bounds__(kThreads, (LO >= 3) ? 1 : 2)
+    tp_message_forward_kernel(const __grid_constant__ CoefParams<Paths<LI, LE, LO>::CT> P) {
   using PS = Paths<LI, LE, LO>;
   constexpr int A = PS::A, B = PS::B, ROWS = PS::ROWS, NP = PS::NP;
+  const TPArgs& a = P.a;
   extern __shared__ __align__(16) float smem[];
-  float* s_coef = smem;
-  int2* s_desc = reinterpret_cast<int2*>(smem + round4(PS::CT));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* s_y = smem + table_floats<PS>() + warp * warp_floats<PS>();
-  float* s_bond = s_y + 32;
-  load_tables<PS>(a, s_coef, s_desc);
-  __syncthreads();
 
   const int C = a.channels;
+  const bool gate_bulk = bulk_rows(a.gates, NP * C * 4), x_bulk = bulk_rows(a.features, A * C * 4);
   const int64_t items = a.rows * a.slices;
   for (int64_t item = (int64_t)blockIdx.x * kWarps + warp; item < items; item += (int64_t)gridDim.x * kWarps) {
     const int64_t n = item / a.slices;
@@ -131,15 +193,6 @@ __global__ void __launch_bounds__(kThreads, (LO >= 3) ? 1 : 2) tp_message_forwar
     for (int r = 0; r < ROWS; ++r)
 #pragma unroll
       for (int ch = 0; ch < CPL; ++ch) acc[r][ch] = 0.f;
-    float w[NP][CPL];
-#pragma unroll
-    for (int p = 0; p < NP; ++p)
-#pragma unroll
-      for (int ch = 0; ch < CPL; ++ch) w[p][ch] = 1.f;
-    if (a.weight && active) {
-#pragma unroll
-      for (int p = 0; p < NP; ++p) load_vec<CPL>(w[p], a.weight + p * C + c0);
-    }
     const int64_t k0 = a.offsets[n], k1 = a.offsets[n + 1];
     int64_t e_lane = 0, s_lane = 0;
     float m_lane = 1.f;
@@ -155,6 +208,12 @@ __global__ void __launch_bounds__(kThreads, (LO >= 3) ? 1 : 2) tp_message_forwar
           s_lane = a.src[e_lane];
           m_lane = a.mask ? __ldg(a.mask + e_lane) : 1.f;
         }
+      }
+      // The lane holding edge k + kAheadL2 of this batch (edges 1..kAheadL2 at a
+      // batch start) pulls its gate row and source row into L2.
+      if (s == 0 && (t == 0 ? (lane >= 1 && lane <= kAheadL2) : lane == t + kAheadL2) && k - t + lane < k1) {
+        if (gate_bulk) prefetch_l2_bulk(a.gates + e_lane * (int64_t)NP * C, NP * C * 4);
+        if (x_bulk) prefetch_l2_bulk(a.features + s_lane * (int64_t)A * C, A * C * 4);
       }
       const int64_t e = __shfl_sync(0xffffffffu, e_lane, t);
       const int64_t xs = __shfl_sync(0xffffffffu, s_lane, t);
@@ -182,33 +241,48 @@ __global__ void __launch_bounds__(kThreads, (LO >= 3) ? 1 : 2) tp_message_forwar
 #pragma unroll
       for (int p = 0; p < NP; ++p)
 #pragma unroll
-        for (int ch = 0; ch < CPL; ++ch) g[p][ch] = gn[p][ch] * w[p][ch] * m;
+        for (int ch = 0; ch < CPL; ++ch) g[p][ch] = gn[p][ch] * m;
       if (lane < B) s_y[lane] = yn;
       if (k + 1 < k1) fetch(k + 1);
       __syncwarp();
-      build_bond<PS>(s_coef, s_desc, s_y, s_bond, lane);
-      __syncwarp();
       static_for<NP>([&](auto pc) {
         constexpr int p = decltype(pc)::value;
-        constexpr int l1 = PS::T.l1[p], l3 = PS::T.l3[p];
+        constexpr int l1 = PS::T.l1[p], l2 = PS::T.l2[p], l3 = PS::T.l3[p];
         constexpr int m1 = 2 * l1 + 1, m3 = 2 * l3 + 1;
-        constexpr int BO = PS::T.bond_off[p], RO = PS::T.out_row[p];
-#pragma unroll
-        for (int kk = 0; kk < m3; ++kk) {
+        constexpr int RO = PS::T.out_row[p], CO = PS::T.coef_off[p];
+        float y[2 * l2 + 1];
+        load_harmonics<l2>(y, s_y);
+        static_for<m3>([&](auto kc) {
+          constexpr int kk = decltype(kc)::value;
           float base[CPL];
 #pragma unroll
           for (int ch = 0; ch < CPL; ++ch) base[ch] = 0.f;
+          static_for<m1>([&](auto ic) {
+            constexpr int i = decltype(ic)::value;
+            if constexpr (BondNonzero<l1, l2, l3, i, kk>::value) {
+              const float b = bond_entry<l1, l2, l3, CO, i, kk>(P.coef, y);
 #pragma unroll
-          for (int i = 0; i < m1; ++i) {
-            const float b = s_bond[BO + i * m3 + kk];
-#pragma unroll
-            for (int ch = 0; ch < CPL; ++ch) base[ch] = fmaf(b, x[l1 * l1 + i][ch], base[ch]);
-          }
+              for (int ch = 0; ch < CPL; ++ch) base[ch] = fmaf(b, x[l1 * l1 + i][ch], base[ch]);
+            }
+          });
 #pragma unroll
           for (int ch = 0; ch < CPL; ++ch) acc[RO + kk][ch] = fmaf(base[ch], g[p][ch], acc[RO + kk][ch]);
-        }
+        });
       });
       __syncwarp();
+    }
+    if (active && a.weight) {
+      // Path weights are constant over the edges: applied once per output block.
+      static_for<NP>([&](auto pc) {
+        constexpr int p = decltype(pc)::value;
+        constexpr int m3 = 2 * PS::T.l3[p] + 1, RO = PS::T.out_row[p];
+        float w[CPL];
+        load_vec<CPL>(w, a.weight + p * C + c0);
+#pragma unroll
+        for (int kk = 0; kk < m3; ++kk)
+#pragma unroll
+          for (int ch = 0; ch < CPL; ++ch) acc[RO + kk][ch] *= w[ch];
+      });
     }
     if (active) {
       float* orow = a.out + n * (int64_t)ROWS * C;
@@ -247,14 +321,17 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
   constexpr int A = PS::A, B = PS::B;
   const TPArgs& a = P.a;
   extern __shared__ __align__(16) float smem[];
-  float* s_coef = smem;
-  int2* s_desc = reinterpret_cast<int2*>(smem + round4(PS::CT));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* s_y = smem + table_floats<PS>() + warp * warp_floats<PS>();
   float* s_bond = s_y + 32;
   float* s_dy = smem + table_floats<PS>() + kWarps * warp_floats<PS>();  // [kWarps][B]
-  load_tables<PS>(a, s_coef, s_desc);
-  __syncthreads();
+  if constexpr (!GRAPH) {
+    // Standalone: the warp builds each instance's bond row once in shared memory
+    // (every entry is read by all its lanes; register-formed entries would raise
+    // the register footprint of the l = 3 variant past its budget).
+    load_tables<PS>(a, smem, reinterpret_cast<int2*>(smem + round4(PS::CT)));
+    __syncthreads();
+  }
 
   const int C = a.channels;
   const int slices = a.slices;
@@ -275,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
     constexpr int XO = decltype(xo)::value;
     constexpr int l1 = PS::T.l1[p], l2 = PS::T.l2[p], l3 = PS::T.l3[p];
     constexpr int m1 = 2 * l1 + 1, m2 = 2 * l2 + 1, m3 = 2 * l3 + 1;
-    constexpr int BO = PS::T.bond_off[p], RO = PS::T.out_row[p], CO = PS::T.coef_off[p];
+    constexpr int RO = PS::T.out_row[p], CO = PS::T.coef_off[p];
     float G[m3][CPL];
     float gate[CPL], w[CPL];
 #pragma unroll
@@ -298,18 +375,28 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
         h[kk][ch] = G[kk][ch] * (gate[ch] * w[ch] * m);
         base[kk][ch] = 0.f;
       }
-    // One read of each bond value serves both the gate adjoint (base) and dx.
+    // Each bond entry (graph: formed in registers; standalone: read from the
+    // instance's bond row) serves both the gate adjoint (base) and dx.
+    constexpr int BO = PS::T.bond_off[p];
+    float y[m2];
+    if constexpr (GRAPH) load_harmonics<l2>(y, s_y);
+    (void)y;
+    static_for<m1>([&](auto ic) {
+      constexpr int i = decltype(ic)::value;
+      static_for<m3>([&](auto kc) {
+        constexpr int kk = decltype(kc)::value;
+        if constexpr (BondNonzero<l1, l2, l3, i, kk>::value) {
+          float b;
+          if constexpr (GRAPH) b = bond_entry<l1, l2, l3, CO, i, kk>(P.coef, y);
+          else b = s_bond[BO + i * m3 + kk];
 #pragma unroll
-    for (int i = 0; i < m1; ++i)
-#pragma unroll
-      for (int kk = 0; kk < m3; ++kk) {
-        const float b = s_bond[BO + i * m3 + kk];
-#pragma unroll
-        for (int ch = 0; ch < CPL; ++ch) {
-          base[kk][ch] = fmaf(b, xl[XO + i][ch], base[kk][ch]);
-          dxl[XO + i][ch] = fmaf(b, h[kk][ch], dxl[XO + i][ch]);
+          for (int ch = 0; ch < CPL; ++ch) {
+            base[kk][ch] = fmaf(b, xl[XO + i][ch], base[kk][ch]);
+            dxl[XO + i][ch] = fmaf(b, h[kk][ch], dxl[XO + i][ch]);
+          }
         }
-      }
+      });
+    });
     if (want_dg) {
       float dg[CPL];
 #pragma unroll
@@ -342,18 +429,16 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
     }
   };
 
-  // dY of one edge: warp all-reduce, then a shared-memory sum over the group's slices.
+  // dY of one edge: warp column sums, then a shared-memory sum over the group's slices.
   auto finish_dy = [&](auto& dyp, int64_t e) {
-    float mine = 0.f;
-#pragma unroll
-    for (int j = 0; j < B; ++j) {
-      const float v = warp_sum(dyp[j]);
-      if (lane == j) mine = v;
-    }
+    constexpr int S = ColumnSum<B>::S;
+    const float total = warp_column_sum<B>(dyp, lane);
+    const int col = lane >> S;
+    const bool owner = (lane & ((1 << S) - 1)) == 0 && col < B;
     if (slices == 1) {
-      if (lane < B) a.grad_harmonics[e * B + lane] = mine;
+      if (owner) a.grad_harmonics[e * B + col] = total;
     } else {
-      if (lane < B) s_dy[warp * B + lane] = mine;
+      if (owner) s_dy[warp * B + col] = total;
       group_barrier(1 + group, 32 * slices);
       if (s == 0 && lane < B) {
         float total = 0.f;
@@ -371,7 +456,7 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
       const int64_t e = node;
       if (lane < B) s_y[lane] = __ldg(a.harmonics + e * B + lane);
       __syncwarp();
-      build_bond<PS>(s_coef, s_desc, s_y, s_bond, lane);
+      build_bond<PS>(smem, reinterpret_cast<const int2*>(smem + round4(PS::CT)), s_y, s_bond, lane);
       __syncwarp();
       float dyp[B];
 #pragma unroll
@@ -398,6 +483,8 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
       __syncwarp();
     } else {
       // Graph: a source node's rows stay in registers while its out-edges are walked.
+      const bool gate_bulk = bulk_rows(a.gates, PS::NP * C * 4);
+      const bool grad_bulk = bulk_rows(a.grad_out, PS::ROWS * C * 4);
       const int64_t k0 = a.offsets[node], k1 = a.offsets[node + 1];
       float x[A][CPL], dx[A][CPL];
 #pragma unroll
@@ -418,6 +505,12 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
             d_lane = a.dst[e_lane];
             m_lane = a.mask ? __ldg(a.mask + e_lane) : 1.f;
           }
+        }
+        // The lane holding edge k + kAheadL2 of this batch (edges 1..kAheadL2 at a
+        // batch start) pulls its gate row and gathered output-gradient row into L2.
+        if (s == 0 && (t == 0 ? (lane >= 1 && lane <= kAheadL2) : lane == t + kAheadL2) && lane < batch) {
+          if (gate_bulk) prefetch_l2_bulk(a.gates + e_lane * (int64_t)PS::NP * C, PS::NP * C * 4);
+          if (grad_bulk) prefetch_l2_bulk(a.grad_out + d_lane * (int64_t)PS::ROWS * C, PS::ROWS * C * 4);
         }
         const int64_t e = __shfl_sync(0xffffffffu, e_lane, t);
         const int64_t d = __shfl_sync(0xffffffffu, d_lane, t);
@@ -440,8 +533,6 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
           }
         }
         if (lane < B) s_y[lane] = __ldg(a.harmonics + e * B + lane);
-        __syncwarp();
-        build_bond<PS>(s_coef, s_desc, s_y, s_bond, lane);
         __syncwarp();
         float dyp[B];
 #pragma unroll
@@ -488,21 +579,22 @@ Variant describe(int cpl, int layout, int kind, int li, int le, int lo) {
 
 template <int LI, int LE, int LO, int CPL, int LAYOUT, int KIND>
 cudaError_t launch_plain(const TPArgs& args, const float*, int grid, int block, size_t smem, cudaStream_t stream) {
-  if constexpr (KIND == kForward)
-    tp_forward_kernel<LI, LE, LO, CPL, LAYOUT><<<grid, block, smem, stream>>>(args);
-  else
-    tp_message_forward_kernel<LI, LE, LO, CPL, LAYOUT><<<grid, block, smem, stream>>>(args);
+  tp_forward_kernel<LI, LE, LO, CPL, LAYOUT><<<grid, block, smem, stream>>>(args);
   return cudaGetLastError();
 }
 
-template <int LI, int LE, int LO, int CPL, int LAYOUT, bool GRAPH>
-cudaError_t launch_adjoint(const TPArgs& args, const float* coef, int grid, int block, size_t smem,
-                           cudaStream_t stream) {
+// Kernels that read the CG table from the parameter bank get it by value.
+template <int LI, int LE, int LO, int CPL, int LAYOUT, int KIND>
+cudaError_t launch_coef(const TPArgs& args, const float* coef, int grid, int block, size_t smem,
+                        cudaStream_t stream) {
   using PS = Paths<LI, LE, LO>;
   CoefParams<PS::CT> params;
   params.a = args;
   for (int t = 0; t < PS::CT; ++t) params.coef[t] = coef[t];
-  tp_adjoint_kernel<LI, LE, LO, CPL, LAYOUT, GRAPH><<<grid, block, smem, stream>>>(params);
+  if constexpr (KIND == kMessageForward)
+    tp_message_forward_kernel<LI, LE, LO, CPL, LAYOUT><<<grid, block, smem, stream>>>(params);
+  else
+    tp_adjoint_kernel<LI, LE, LO, CPL, LAYOUT, KIND == kMessageAdjoint><<<grid, block, smem, stream>>>(params);
   return cudaGetLastError();
 }
 
@@ -515,11 +607,10 @@ Variant make_variant() {
     v.launch = launch_plain<LI, LE, LO, CPL, LAYOUT, KIND>;
   } else if constexpr (KIND == kMessageForward) {
     v.fn = (const void*)tp_message_forward_kernel<LI, LE, LO, CPL, LAYOUT>;
-    v.launch = launch_plain<LI, LE, LO, CPL, LAYOUT, KIND>;
+    v.launch = launch_coef<LI, LE, LO, CPL, LAYOUT, KIND>;
   } else {
-    constexpr bool graph = KIND == kMessageAdjoint;
-    v.fn = (const void*)tp_adjoint_kernel<LI, LE, LO, CPL, LAYOUT, graph>;
-    v.launch = launch_adjoint<LI, LE, LO, CPL, LAYOUT, graph>;
+    v.fn = (const void*)tp_adjoint_kernel<LI, LE, LO, CPL, LAYOUT, KIND == kMessageAdjoint>;
+    v.launch = launch_coef<LI, LE, LO, CPL, LAYOUT, KIND>;
   }
   return v;
 }

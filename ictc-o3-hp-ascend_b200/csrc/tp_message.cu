@@ -7,8 +7,8 @@ namespace ictc {
 
 template <int LI, int LE, int LO, int LAYOUT>
 static void add_message(std::vector<Variant>& out) {
+  // The forward keeps a node's whole output row in registers: one channel per lane.
   out.push_back(make_variant<LI, LE, LO, 1, LAYOUT, kMessageForward>());
-  out.push_back(make_variant<LI, LE, LO, 2, LAYOUT, kMessageForward>());
   out.push_back(make_variant<LI, LE, LO, 1, LAYOUT, kMessageAdjoint>());
   out.push_back(make_variant<LI, LE, LO, 2, LAYOUT, kMessageAdjoint>());
 }
