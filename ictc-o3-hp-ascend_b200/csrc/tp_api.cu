@@ -36,9 +36,12 @@ struct ictc_tp_plan {
   int channels, li, le, lo, layout;
   const Variant* v[kKinds];
   int cpl[kKinds], slices[kKinds], block[kKinds], grid[kKinds];
+  size_t smem[kKinds];
+  int stage_floats;         // graph adjoint staging buffer per warp (0 = not staged)
   std::vector<float> coef;  // host copy of the dense CG table (kernel-parameter source)
   float* d_coef;
   int2* d_desc;
+  int* d_status;            // non-zero after a kernel gave up on a timed-out wait
   int device;
 };
 
@@ -116,6 +119,7 @@ extern "C" int ictc_tp_plan_create(int channels, int input_lmax, int edge_lmax, 
     }
     plan->cpl[kind] = cpl;
     plan->slices[kind] = (channels + 32 * cpl - 1) / (32 * cpl);
+    plan->smem[kind] = plan->v[kind]->smem;
     plan->block[kind] = (kind == kAdjoint || kind == kMessageAdjoint)
                             ? 32 * plan->slices[kind] * (kWarps / plan->slices[kind])
                             : kThreads;
@@ -159,27 +163,41 @@ extern "C" int ictc_tp_plan_create(int channels, int input_lmax, int edge_lmax, 
       }
     src += (int64_t)m1 * m2 * m3;
   }
+  // The graph adjoint stages each edge's output-gradient and gate rows in shared
+  // memory when a node is one warp and the rows are whole 16-byte units that fit.
+  {
+    const Variant* va = plan->v[kMessageAdjoint];
+    const int stage = (va->rows + va->np) * channels;
+    const bool fits = plan->slices[kMessageAdjoint] == 1 && (va->rows * channels) % 4 == 0 &&
+                      (va->np * channels) % 4 == 0 && stage * 4 <= kStageBudgetBytes;
+    plan->stage_floats = fits ? stage : 0;
+    if (fits) plan->smem[kMessageAdjoint] = staged_smem_bytes((int)va->smem, stage);
+  }
   plan->coef = coef;
   cudaGetDevice(&plan->device);
   plan->d_coef = nullptr;
   plan->d_desc = nullptr;
+  plan->d_status = nullptr;
   if (cudaMalloc(&plan->d_coef, sizeof(float) * (coef.size() + 4)) != cudaSuccess ||
-      cudaMalloc(&plan->d_desc, sizeof(int2) * (desc.size() + 4)) != cudaSuccess) {
+      cudaMalloc(&plan->d_desc, sizeof(int2) * (desc.size() + 4)) != cudaSuccess ||
+      cudaMalloc(&plan->d_status, sizeof(int)) != cudaSuccess) {
     cudaGetLastError();
     cudaFree(plan->d_coef);
+    cudaFree(plan->d_desc);
     delete plan;
     ictc_set_error("ictc_tp_plan_create: device allocation failed%s", "");
     return ICTC_ERR_NOMEM;
   }
   cudaMemcpy(plan->d_coef, coef.data(), sizeof(float) * coef.size(), cudaMemcpyHostToDevice);
   cudaMemcpy(plan->d_desc, desc.data(), sizeof(int2) * desc.size(), cudaMemcpyHostToDevice);
+  cudaMemset(plan->d_status, 0, sizeof(int));
   int sms = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, plan->device);
   for (int kind = 0; kind < kKinds; ++kind) {
     const Variant* v = plan->v[kind];
     int per_sm = 0;
-    cudaFuncSetAttribute(v->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)v->smem);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v->fn, plan->block[kind], v->smem);
+    cudaFuncSetAttribute(v->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan->smem[kind]);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v->fn, plan->block[kind], plan->smem[kind]);
     plan->grid[kind] = sms * (per_sm < 1 ? 1 : per_sm);
   }
   cudaError_t err = cudaGetLastError();
@@ -187,6 +205,7 @@ extern "C" int ictc_tp_plan_create(int channels, int input_lmax, int edge_lmax, 
     ictc_set_error("ictc_tp_plan_create: %s", cudaGetErrorString(err));
     cudaFree(plan->d_coef);
     cudaFree(plan->d_desc);
+    cudaFree(plan->d_status);
     delete plan;
     return ICTC_ERR_CUDA;
   }
@@ -198,7 +217,24 @@ extern "C" int ictc_tp_plan_destroy(ictc_tp_plan* plan) {
   if (!plan) return ICTC_OK;
   cudaFree(plan->d_coef);
   cudaFree(plan->d_desc);
+  cudaFree(plan->d_status);
   delete plan;
+  return ICTC_OK;
+}
+
+extern "C" int ictc_tp_plan_status(const ictc_tp_plan* plan, int32_t* status, int reset) {
+  if (!plan || !status) {
+    ictc_set_error("ictc_tp_plan_status: invalid (null) argument%s", "");
+    return ICTC_ERR_INVALID;
+  }
+  int value = 0;
+  cudaError_t err = cudaMemcpy(&value, plan->d_status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (err == cudaSuccess && reset) err = cudaMemset(plan->d_status, 0, sizeof(int));
+  if (err != cudaSuccess) {
+    ictc_set_error("ictc_tp_plan_status: %s", cudaGetErrorString(err));
+    return ICTC_ERR_CUDA;
+  }
+  *status = value;
   return ICTC_OK;
 }
 
@@ -222,12 +258,19 @@ static int launch(const ictc_tp_plan* plan, int kind, TPArgs& args, int64_t unit
   args.desc = plan->d_desc;
   args.channels = plan->channels;
   args.slices = plan->slices[kind];
+  args.status = plan->d_status;
+  args.stage_floats = 0;
+  if (kind == kMessageAdjoint && plan->stage_floats > 0 &&
+      (reinterpret_cast<uintptr_t>(args.grad_out) & 15u) == 0 &&
+      (reinterpret_cast<uintptr_t>(args.gates) & 15u) == 0)
+    args.stage_floats = plan->stage_floats;
   if (args.rows <= 0) return ICTC_OK;
   int64_t work = (args.rows * (kind == kAdjoint || kind == kMessageAdjoint ? 1 : args.slices) + units_per_block - 1) /
                  units_per_block;
   int grid = (int)(work < plan->grid[kind] ? work : plan->grid[kind]);
   const Variant* v = plan->v[kind];
-  cudaError_t err = v->launch(args, plan->coef.data(), grid, plan->block[kind], v->smem, (cudaStream_t)stream);
+  cudaError_t err = v->launch(args, plan->coef.data(), grid, plan->block[kind], plan->smem[kind],
+                              (cudaStream_t)stream);
   if (err != cudaSuccess) {
     ictc_set_error(what, cudaGetErrorString(err));
     return ICTC_ERR_CUDA;

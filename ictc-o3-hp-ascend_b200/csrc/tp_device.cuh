@@ -34,6 +34,8 @@ struct TPArgs {
   int64_t rows;                         // instances (standalone) or CSR nodes (graph)
   int channels;
   int slices;                           // ceil(C / (32 * CPL))
+  int stage_floats;                     // graph adjoint: per-warp staging buffer (0 = not staged)
+  int* status;                          // device status word: non-zero after a timed-out wait
 };
 
 // Kernel parameters of the adjoint kernels: the launch arguments plus the dense
@@ -66,6 +68,17 @@ template <class PS>
 __host__ __device__ constexpr int smem_floats() {
   return table_floats<PS>() + kWarps * warp_floats<PS>() + kWarps * PS::B;  // + dY partials
 }
+
+// Graph adjoint staging area, after the kernel's regular shared memory: one
+// mbarrier per warp (128 B), then one buffer of stage_floats per warp.
+__host__ __device__ constexpr int stage_offset_bytes(int regular_bytes) { return (regular_bytes + 127) & ~127; }
+__host__ __device__ constexpr int staged_smem_bytes(int regular_bytes, int stage_floats) {
+  return stage_offset_bytes(regular_bytes) + 128 + kWarps * stage_floats * 4;
+}
+// Largest staged edge (output-gradient row + gate row) per warp.
+constexpr int kStageBudgetBytes = 12288;
+// Time limit of a staging wait.
+constexpr uint64_t kStageWaitNs = 2000000000ull;
 
 template <class PS>
 __device__ __forceinline__ void load_tables(const TPArgs& a, float* s_coef, int2* s_desc) {
@@ -169,6 +182,50 @@ __device__ __forceinline__ void store_features(float* row, const float (&x)[(LI 
       for (int ch = 0; ch < CPL; ++ch)
 #pragma unroll
         for (int i = 0; i < 2 * l + 1; ++i) row[l * l * channels + (c0 + ch) * (2 * l + 1) + i] = x[l * l + i][ch];
+  }
+}
+
+// Vector load of CPL consecutive floats from shared memory.
+template <int CPL>
+__device__ __forceinline__ void load_vec_shared(float (&dst)[CPL], const float* src) {
+  if constexpr (CPL == 4) {
+    const float4 t = *reinterpret_cast<const float4*>(src);
+    dst[0] = t.x; dst[1] = t.y; dst[2] = t.z; dst[3] = t.w;
+  } else if constexpr (CPL == 2) {
+    const float2 t = *reinterpret_cast<const float2*>(src);
+    dst[0] = t.x; dst[1] = t.y;
+  } else {
+    dst[0] = src[0];
+  }
+}
+
+// The m3 x CPL output block of one path from a packed output row staged in
+// shared memory.  mul_ir: the lane's CPL channels are 2 m3 consecutive floats,
+// read as float2 (c0 and the block offset are even when CPL = 2).
+template <int CPL, int LAYOUT, int RO, int m3>
+__device__ __forceinline__ void load_out_block_shared(float (&G)[m3][CPL], const float* row, int channels,
+                                                      int c0) {
+  if constexpr (LAYOUT == kIrMul) {
+#pragma unroll
+    for (int k = 0; k < m3; ++k) load_vec_shared<CPL>(G[k], row + (RO + k) * channels + c0);
+  } else if constexpr (CPL == 2) {
+    const float* blk = row + RO * channels + c0 * m3;
+    float t[2 * m3];
+#pragma unroll
+    for (int q = 0; q < m3; ++q) {
+      const float2 v = *reinterpret_cast<const float2*>(blk + 2 * q);
+      t[2 * q] = v.x;
+      t[2 * q + 1] = v.y;
+    }
+#pragma unroll
+    for (int ch = 0; ch < 2; ++ch)
+#pragma unroll
+      for (int k = 0; k < m3; ++k) G[k][ch] = t[ch * m3 + k];
+  } else {
+#pragma unroll
+    for (int ch = 0; ch < CPL; ++ch)
+#pragma unroll
+      for (int k = 0; k < m3; ++k) G[k][ch] = row[RO * channels + (c0 + ch) * m3 + k];
   }
 }
 

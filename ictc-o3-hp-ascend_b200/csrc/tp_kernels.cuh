@@ -12,6 +12,7 @@
 #pragma once
 
 #include "cg_pattern.h"
+#include "tc_sm100.cuh"
 #include "tp_device.cuh"
 
 namespace ictc {
@@ -346,7 +347,8 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
   // Adjoint of one path for one edge.  Rows XO + i of xl / dxl hold the path's
   // input degree and its gradient accumulators (XO = l1^2 for whole-row arrays,
   // 0 for one-degree arrays); dyp: this lane's partial dY of the edge.
-  auto path_adjoint = [&](auto pc, auto xo, auto& xl, auto& dxl, auto& dyp, const float* Grow,
+  // Grow / grow point into this warp's shared staging buffer when `staged`.
+  auto path_adjoint = [&](auto pc, auto xo, auto staged, auto& xl, auto& dxl, auto& dyp, const float* Grow,
                           const float* grow, float* dgrow, float m) {
     constexpr int p = decltype(pc)::value;
     constexpr int XO = decltype(xo)::value;
@@ -358,8 +360,13 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
 #pragma unroll
     for (int ch = 0; ch < CPL; ++ch) { gate[ch] = 1.f; w[ch] = 1.f; }
     if (active) {
-      load_out_block<CPL, LAYOUT, RO, m3>(G, Grow, C, c0, !GRAPH);
-      if (grow) load_vec_stream<CPL>(gate, grow + p * C + c0);
+      if constexpr (decltype(staged)::value) {
+        load_out_block_shared<CPL, LAYOUT, RO, m3>(G, Grow, C, c0);
+        if (grow) load_vec_shared<CPL>(gate, grow + p * C + c0);
+      } else {
+        load_out_block<CPL, LAYOUT, RO, m3>(G, Grow, C, c0, !GRAPH);
+        if (grow) load_vec_stream<CPL>(gate, grow + p * C + c0);
+      }
       if (a.weight) load_vec<CPL>(w, a.weight + p * C + c0);
     } else {
 #pragma unroll
@@ -378,6 +385,7 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
     // Each bond entry (graph: formed in registers; standalone: read from the
     // instance's bond row) serves both the gate adjoint (base) and dx.
     constexpr int BO = PS::T.bond_off[p];
+    (void)BO;
     float y[m2];
     if constexpr (GRAPH) load_harmonics<l2>(y, s_y);
     (void)y;
@@ -449,6 +457,29 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
     }
   };
 
+  // Graph adjoint staging (one warp per node): each edge's output-gradient row and
+  // gate row arrive in this warp's shared buffer by bulk copy, completed on its
+  // mbarrier; the copy of the next edge is issued as soon as the buffer is free.
+  const bool staged = GRAPH && a.stage_floats > 0;
+  uint64_t* s_bar = nullptr;
+  float* s_stage = nullptr;
+  uint32_t phase = 0;
+  if (staged) {
+    char* base = reinterpret_cast<char*>(smem) + stage_offset_bytes((int)(smem_floats<PS>() * sizeof(float)));
+    s_bar = reinterpret_cast<uint64_t*>(base) + warp;
+    s_stage = reinterpret_cast<float*>(base + 128) + warp * a.stage_floats;
+    if (lane == 0) tc::mbar_init(s_bar, 1);
+    __syncwarp();
+  }
+  auto stage_issue = [&](int64_t e, int64_t d) {
+    if (lane == 0) {
+      const uint32_t gbytes = PS::ROWS * C * 4, tbytes = a.gates ? PS::NP * C * 4 : 0;
+      tc::mbar_arrive_expect(s_bar, gbytes + tbytes);
+      tc::bulk_load(s_stage, a.grad_out + d * (int64_t)PS::ROWS * C, gbytes, s_bar);
+      if (tbytes) tc::bulk_load(s_stage + PS::ROWS * C, a.gates + e * (int64_t)PS::NP * C, tbytes, s_bar);
+    }
+  };
+
   for (int64_t node = (int64_t)blockIdx.x * groups + group; node < a.rows; node += (int64_t)gridDim.x * groups) {
     if constexpr (!GRAPH) {
       // Standalone: one instance; paths are ordered by input degree, so one
@@ -475,7 +506,8 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
           for (int ch = 0; ch < CPL; ++ch) dxl[i][ch] = 0.f;
         static_for<PS::NP>([&](auto pc) {
           if constexpr (PS::T.l1[decltype(pc)::value] == decltype(lc)::value)
-            path_adjoint(pc, std::integral_constant<int, 0>{}, xl, dxl, dyp, Grow, grow, dgrow, 1.f);
+            path_adjoint(pc, std::integral_constant<int, 0>{}, std::false_type{}, xl, dxl, dyp, Grow, grow, dgrow,
+                         1.f);
         });
         if (want_dx && active) store_degree<l1, CPL, LAYOUT>(a.grad_features + e * A * C, dxl, C, c0);
       });
@@ -484,7 +516,6 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
     } else {
       // Graph: a source node's rows stay in registers while its out-edges are walked.
       const bool gate_bulk = bulk_rows(a.gates, PS::NP * C * 4);
-      const bool grad_bulk = bulk_rows(a.grad_out, PS::ROWS * C * 4);
       const int64_t k0 = a.offsets[node], k1 = a.offsets[node + 1];
       float x[A][CPL], dx[A][CPL];
 #pragma unroll
@@ -495,6 +526,7 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
       int64_t e_lane = 0, d_lane = 0;
       float m_lane = 1.f;
       int batch = 0;
+      bool pending = false;  // staged: the copy of edge k is already in flight
       for (int64_t k = k0; k < k1; ++k) {
         const int t = (int)((k - k0) & 31);
         if (t == 0) {
@@ -507,15 +539,26 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
           }
         }
         // The lane holding edge k + kAheadL2 of this batch (edges 1..kAheadL2 at a
-        // batch start) pulls its gate row and gathered output-gradient row into L2.
-        if (s == 0 && (t == 0 ? (lane >= 1 && lane <= kAheadL2) : lane == t + kAheadL2) && lane < batch) {
-          if (gate_bulk) prefetch_l2_bulk(a.gates + e_lane * (int64_t)PS::NP * C, PS::NP * C * 4);
-          if (grad_bulk) prefetch_l2_bulk(a.grad_out + d_lane * (int64_t)PS::ROWS * C, PS::ROWS * C * 4);
-        }
+        // batch start) pulls its streamed gate row into L2.
+        if (gate_bulk && s == 0 && (t == 0 ? (lane >= 1 && lane <= kAheadL2) : lane == t + kAheadL2) &&
+            lane < batch)
+          prefetch_l2_bulk(a.gates + e_lane * (int64_t)PS::NP * C, PS::NP * C * 4);
         const int64_t e = __shfl_sync(0xffffffffu, e_lane, t);
         const int64_t d = __shfl_sync(0xffffffffu, d_lane, t);
         const float m = __shfl_sync(0xffffffffu, m_lane, t);
-        {
+        if (staged) {
+          if (!pending) stage_issue(e, d);
+          bool ok = tc::mbar_wait(s_bar, phase, kStageWaitNs);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) {
+            // Lost copy: record it, give the copy in flight a last bounded chance to
+            // land (the buffer must not be written after the warp leaves), and stop.
+            if (lane == 0 && a.status) atomicExch(a.status, 1);
+            tc::mbar_wait(s_bar, phase, kStageWaitNs);
+            return;
+          }
+          phase ^= 1u;
+        } else {
           // Pull the next edge's gathered output-gradient row and gate row into L1
           // while this edge computes; the group's slices split the lines.
           const int tn = t + 1 < batch ? t + 1 : t;
@@ -537,13 +580,31 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
         float dyp[B];
 #pragma unroll
         for (int j = 0; j < B; ++j) dyp[j] = 0.f;
-        const float* Grow = a.grad_out + d * (int64_t)PS::ROWS * C;
-        const float* grow = a.gates ? a.gates + e * (int64_t)PS::NP * C : nullptr;
         float* dgrow = want_dg ? a.grad_gates + e * (int64_t)PS::NP * C : nullptr;
-        static_for<PS::NP>([&](auto pc) {
-          constexpr int l1 = PS::T.l1[decltype(pc)::value];
-          path_adjoint(pc, std::integral_constant<int, l1 * l1>{}, x, dx, dyp, Grow, grow, dgrow, m);
-        });
+        if (staged) {
+          const float* grow = a.gates ? s_stage + PS::ROWS * C : nullptr;
+          static_for<PS::NP>([&](auto pc) {
+            constexpr int l1 = PS::T.l1[decltype(pc)::value];
+            path_adjoint(pc, std::integral_constant<int, l1 * l1>{}, std::true_type{}, x, dx, dyp, s_stage, grow,
+                         dgrow, m);
+          });
+          // Every staged value has been consumed (in-order issue): the buffer is free.
+          __syncwarp();
+          pending = k + 1 < k1 && t + 1 < batch;
+          if (pending) {
+            const int64_t en = __shfl_sync(0xffffffffu, e_lane, t + 1);
+            const int64_t dn = __shfl_sync(0xffffffffu, d_lane, t + 1);
+            stage_issue(en, dn);
+          }
+        } else {
+          const float* Grow = a.grad_out + d * (int64_t)PS::ROWS * C;
+          const float* grow = a.gates ? a.gates + e * (int64_t)PS::NP * C : nullptr;
+          static_for<PS::NP>([&](auto pc) {
+            constexpr int l1 = PS::T.l1[decltype(pc)::value];
+            path_adjoint(pc, std::integral_constant<int, l1 * l1>{}, std::false_type{}, x, dx, dyp, Grow, grow,
+                         dgrow, m);
+          });
+        }
         if (want_dy) finish_dy(dyp, e);
         __syncwarp();
       }

@@ -12,7 +12,7 @@ import threading
 import torch
 
 LIBRARY_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libictc_cuda.so")
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int
@@ -25,6 +25,7 @@ _SIGNATURES = {
     "ictc_tp_plan_create": [_i, _i, _i, _i, _i, _i, _p, _p, _i64, _i, _i, ctypes.POINTER(_p)],
     "ictc_tp_plan_destroy": [_p],
     "ictc_tp_plan_info": [_p, ctypes.POINTER(_i64), _i],
+    "ictc_tp_plan_status": [_p, ctypes.POINTER(ctypes.c_int32), _i],
     "ictc_tp_forward": [_p, _p, _p, _p, _p, _p, _i64, _p],
     "ictc_tp_backward": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p],
     "ictc_tp_message_forward": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p],

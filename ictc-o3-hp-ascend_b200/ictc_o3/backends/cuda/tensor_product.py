@@ -62,6 +62,18 @@ class TPPlan:
         _native.call("ictc_tp_plan_info", handle, extra, 12)
         self.cpl_message_forward, self.cpl_message_backward = int(extra[8]), int(extra[9])
 
+    def status(self, reset: bool = False) -> int:
+        """Non-zero when a kernel of this plan gave up on a timed-out wait (one device read)."""
+        value = ctypes.c_int32()
+        _native.call("ictc_tp_plan_status", self.handle, ctypes.byref(value), int(reset))
+        return int(value.value)
+
+    def check_status(self):
+        """Raise if a kernel of this plan recorded a timed-out wait."""
+        code = self.status()
+        if code:
+            raise RuntimeError(f"tensor-product kernel reported error {code} (timed-out staging wait)")
+
     def __del__(self):
         handle = getattr(self, "handle", None)
         if handle is not None and _native._lib is not None:

@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define ICTC_ABI_VERSION 1
+#define ICTC_ABI_VERSION 2
 
 #define ICTC_OK 0
 #define ICTC_ERR_INVALID (-1)     /* bad pointer, size or shape            */
@@ -69,6 +69,13 @@ int ictc_tp_plan_destroy(ictc_tp_plan* plan);
  * feature_width, harmonic_width, cpl_forward, cpl_backward, forward grid,
  * cpl_message_forward, cpl_message_backward, adjoint grid, adjoint block]. */
 int ictc_tp_plan_info(const ictc_tp_plan* plan, int64_t* info, int n);
+
+/* Status word of the plan's kernels: *status = 0, or non-zero after a kernel
+ * gave up on a timed-out wait (the graph adjoint's staged row copies); the
+ * kernel then leaves its remaining work undone.  Reads one int from the device
+ * (synchronising); reset != 0 clears the word.  No reference counterpart: the
+ * reference backends have no asynchronous copies to lose. */
+int ictc_tp_plan_status(const ictc_tp_plan* plan, int32_t* status, int reset);
 
 /*
  * TP forward, out = TP(features, harmonics, gates * weight).
