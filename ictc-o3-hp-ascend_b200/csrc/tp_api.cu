@@ -38,6 +38,11 @@ struct ictc_tp_plan {
   int cpl[kKinds], slices[kKinds], block[kKinds], grid[kKinds];
   size_t smem[kKinds];
   int stage_floats;         // graph adjoint staging buffer per warp (0 = not staged)
+  // Staged graph forward, two channels per lane (one warp per node), used when
+  // the feature and gate rows of a launch are 16-byte aligned; else v[kMessageForward].
+  const Variant* fwd2;
+  int fwd2_stage_floats, fwd2_grid;
+  size_t fwd2_smem;
   std::vector<float> coef;  // host copy of the dense CG table (kernel-parameter source)
   float* d_coef;
   int2* d_desc;
@@ -173,6 +178,18 @@ extern "C" int ictc_tp_plan_create(int channels, int input_lmax, int edge_lmax, 
     plan->stage_floats = fits ? stage : 0;
     if (fits) plan->smem[kMessageAdjoint] = staged_smem_bytes((int)va->smem, stage);
   }
+  plan->fwd2 = nullptr;
+  plan->fwd2_stage_floats = plan->fwd2_grid = 0;
+  plan->fwd2_smem = 0;
+  if (channels == 64) {
+    const Variant* v2 = find_variant(input_lmax, edge_lmax, output_lmax, 2, layout, kMessageForward);
+    if (v2 && (v2->a * channels) % 4 == 0 && (v2->np * channels) % 4 == 0 &&
+        2 * (v2->a + v2->np) * channels * 4 <= 2 * kStageBudgetBytes) {
+      plan->fwd2 = v2;
+      plan->fwd2_stage_floats = (v2->a + v2->np) * channels;
+      plan->fwd2_smem = staged_smem_bytes((int)v2->smem, 2 * plan->fwd2_stage_floats);
+    }
+  }
   plan->coef = coef;
   cudaGetDevice(&plan->device);
   plan->d_coef = nullptr;
@@ -199,6 +216,12 @@ extern "C" int ictc_tp_plan_create(int channels, int input_lmax, int edge_lmax, 
     cudaFuncSetAttribute(v->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan->smem[kind]);
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v->fn, plan->block[kind], plan->smem[kind]);
     plan->grid[kind] = sms * (per_sm < 1 ? 1 : per_sm);
+  }
+  if (plan->fwd2) {
+    int per_sm = 0;
+    cudaFuncSetAttribute(plan->fwd2->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan->fwd2_smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, plan->fwd2->fn, kThreads, plan->fwd2_smem);
+    plan->fwd2_grid = sms * (per_sm < 1 ? 1 : per_sm);
   }
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) {
@@ -260,6 +283,17 @@ static int launch(const ictc_tp_plan* plan, int kind, TPArgs& args, int64_t unit
   args.slices = plan->slices[kind];
   args.status = plan->d_status;
   args.stage_floats = 0;
+  const Variant* v = plan->v[kind];
+  int grid_cap = plan->grid[kind];
+  size_t smem = plan->smem[kind];
+  if (kind == kMessageForward && plan->fwd2 && (reinterpret_cast<uintptr_t>(args.features) & 15u) == 0 &&
+      (reinterpret_cast<uintptr_t>(args.gates) & 15u) == 0) {
+    v = plan->fwd2;
+    grid_cap = plan->fwd2_grid;
+    smem = plan->fwd2_smem;
+    args.slices = 1;
+    args.stage_floats = plan->fwd2_stage_floats;
+  }
   if (kind == kMessageAdjoint && plan->stage_floats > 0 &&
       (reinterpret_cast<uintptr_t>(args.grad_out) & 15u) == 0 &&
       (reinterpret_cast<uintptr_t>(args.gates) & 15u) == 0)
@@ -267,10 +301,8 @@ static int launch(const ictc_tp_plan* plan, int kind, TPArgs& args, int64_t unit
   if (args.rows <= 0) return ICTC_OK;
   int64_t work = (args.rows * (kind == kAdjoint || kind == kMessageAdjoint ? 1 : args.slices) + units_per_block - 1) /
                  units_per_block;
-  int grid = (int)(work < plan->grid[kind] ? work : plan->grid[kind]);
-  const Variant* v = plan->v[kind];
-  cudaError_t err = v->launch(args, plan->coef.data(), grid, plan->block[kind], plan->smem[kind],
-                              (cudaStream_t)stream);
+  int grid = (int)(work < grid_cap ? work : grid_cap);
+  cudaError_t err = v->launch(args, plan->coef.data(), grid, plan->block[kind], smem, (cudaStream_t)stream);
   if (err != cudaSuccess) {
     ictc_set_error(what, cudaGetErrorString(err));
     return ICTC_ERR_CUDA;

@@ -229,6 +229,47 @@ __device__ __forceinline__ void load_out_block_shared(float (&G)[m3][CPL], const
   }
 }
 
+// All input rows of the lane's channels from a packed feature row staged in
+// shared memory (mul_ir, CPL = 2: float2 reads of each degree's 2 m floats).
+template <int LI, int CPL, int LAYOUT>
+__device__ __forceinline__ void load_features_shared(float (&x)[(LI + 1) * (LI + 1)][CPL], const float* row,
+                                                     int channels, int c0, bool active) {
+  if (!active) {
+#pragma unroll
+    for (int r = 0; r < (LI + 1) * (LI + 1); ++r)
+#pragma unroll
+      for (int ch = 0; ch < CPL; ++ch) x[r][ch] = 0.f;
+    return;
+  }
+  if constexpr (LAYOUT == kIrMul) {
+#pragma unroll
+    for (int r = 0; r < (LI + 1) * (LI + 1); ++r) load_vec_shared<CPL>(x[r], row + r * channels + c0);
+  } else {
+    static_for<LI + 1>([&](auto lc) {
+      constexpr int l = decltype(lc)::value, m = 2 * l + 1;
+      const float* blk = row + l * l * channels + c0 * m;
+      if constexpr (CPL == 2) {
+        float t[2 * m];
+#pragma unroll
+        for (int q = 0; q < m; ++q) {
+          const float2 v = *reinterpret_cast<const float2*>(blk + 2 * q);
+          t[2 * q] = v.x;
+          t[2 * q + 1] = v.y;
+        }
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch)
+#pragma unroll
+          for (int i = 0; i < m; ++i) x[l * l + i][ch] = t[ch * m + i];
+      } else {
+#pragma unroll
+        for (int ch = 0; ch < CPL; ++ch)
+#pragma unroll
+          for (int i = 0; i < m; ++i) x[l * l + i][ch] = blk[ch * m + i];
+      }
+    });
+  }
+}
+
 // Load the m3 x CPL output block of one path from a packed output row.
 template <int CPL, int LAYOUT, int RO, int m3>
 __device__ __forceinline__ void load_out_block(float (&G)[m3][CPL], const float* row, int channels, int c0,

@@ -166,10 +166,14 @@ __global__ void __launch_bounds__(kThreads) tp_forward_kernel(TPArgs a) {
 
 // ---------------------------------------------------------------------------
 // Graph-message forward over a destination CSR: one warp per (destination
-// node, channel slice); the node's whole output row lives in registers.  The
-// edge loop is software-pipelined: the next edge's source row, gate row and
-// harmonics are loaded while the current edge is computed, and edge/source ids
-// arrive in lane-parallel batches of 32.
+// node, channel slice); the node's whole output row lives in registers.  Edge
+// and source ids arrive in lane-parallel batches of 32.  Two ways to feed the
+// edge loop:
+//   * staged (one warp per node, rows in whole 16-byte units): a per-warp ring
+//     of two shared buffers; the source row and gate row of edge k + 1 are
+//     bulk-copied while edge k is computed (bounded mbarrier waits);
+//   * direct: the next edge's source row, gate row and harmonics are loaded
+//     into registers while the current edge is computed.
 // ---------------------------------------------------------------------------
 template <int LI, int LE, int LO, int CPL, int LAYOUT>
 __global__ void __launch_bounds__(kThreads, (LO >= 3) ? 1 : 2)
@@ -183,6 +187,38 @@ __global__ void __launch_bounds__(kThreads, (LO >= 3) ? 1 : 2)
 
   const int C = a.channels;
   const bool gate_bulk = bulk_rows(a.gates, NP * C * 4), x_bulk = bulk_rows(a.features, A * C * 4);
+  const bool staged = a.stage_floats > 0;
+  uint64_t* s_bar = nullptr;
+  float* s_stage = nullptr;
+  uint32_t phases = 0, turn = 0;
+  if (staged) {
+    char* base = reinterpret_cast<char*>(smem) + stage_offset_bytes((int)(smem_floats<PS>() * sizeof(float)));
+    s_bar = reinterpret_cast<uint64_t*>(base) + 2 * warp;
+    s_stage = reinterpret_cast<float*>(base + 128) + 2 * warp * a.stage_floats;
+    if (lane == 0) {
+      tc::mbar_init(s_bar, 1);
+      tc::mbar_init(s_bar + 1, 1);
+    }
+    __syncwarp();
+  }
+  if constexpr (CPL > 1) {
+    // Two channels per lane leave no registers for the direct path's pipeline:
+    // the host launches this width only with staged rows.
+    if (!staged) {
+      if (threadIdx.x == 0 && a.status) atomicExch(a.status, 2);
+      return;
+    }
+  }
+  auto stage_issue = [&](int slot, int64_t e, int64_t xs) {
+    if (lane == 0) {
+      const uint32_t xbytes = A * C * 4, gbytes = a.gates ? NP * C * 4 : 0;
+      float* buf = s_stage + slot * a.stage_floats;
+      tc::mbar_arrive_expect(s_bar + slot, xbytes + gbytes);
+      tc::bulk_load(buf, a.features + xs * (int64_t)A * C, xbytes, s_bar + slot);
+      if (gbytes) tc::bulk_load(buf + A * C, a.gates + e * (int64_t)NP * C, gbytes, s_bar + slot);
+    }
+  };
+
   const int64_t items = a.rows * a.slices;
   for (int64_t item = (int64_t)blockIdx.x * kWarps + warp; item < items; item += (int64_t)gridDim.x * kWarps) {
     const int64_t n = item / a.slices;
@@ -197,80 +233,140 @@ __global__ void __launch_bounds__(kThreads, (LO >= 3) ? 1 : 2)
     const int64_t k0 = a.offsets[n], k1 = a.offsets[n + 1];
     int64_t e_lane = 0, s_lane = 0;
     float m_lane = 1.f;
-    // Registers of the edge being prefetched.
-    float xn[A][CPL], gn[NP][CPL];
-    float yn = 0.f, mn = 1.f;
-    auto fetch = [&](int64_t k) {
-      const int t = (int)((k - k0) & 31);
+    int batch = 0;
+    // Lane-parallel ids of the batch starting at edge k; the lane holding edge
+    // k + kAheadL2 of the batch (edges 1..kAheadL2 at its start) pulls its gate
+    // row and source row into L2.
+    auto batch_ids = [&](int64_t k, int t) {
       if (t == 0) {
         const int64_t kl = k + lane;
+        batch = (int)min((int64_t)32, k1 - k);
         if (kl < k1) {
           e_lane = a.order ? a.order[kl] : kl;
           s_lane = a.src[e_lane];
           m_lane = a.mask ? __ldg(a.mask + e_lane) : 1.f;
         }
       }
-      // The lane holding edge k + kAheadL2 of this batch (edges 1..kAheadL2 at a
-      // batch start) pulls its gate row and source row into L2.
-      if (s == 0 && (t == 0 ? (lane >= 1 && lane <= kAheadL2) : lane == t + kAheadL2) && k - t + lane < k1) {
+      if (s == 0 && (t == 0 ? (lane >= 1 && lane <= kAheadL2) : lane == t + kAheadL2) && lane < batch) {
         if (gate_bulk) prefetch_l2_bulk(a.gates + e_lane * (int64_t)NP * C, NP * C * 4);
         if (x_bulk) prefetch_l2_bulk(a.features + s_lane * (int64_t)A * C, A * C * 4);
       }
-      const int64_t e = __shfl_sync(0xffffffffu, e_lane, t);
-      const int64_t xs = __shfl_sync(0xffffffffu, s_lane, t);
-      mn = __shfl_sync(0xffffffffu, m_lane, t);
-      yn = lane < B ? __ldg(a.harmonics + e * B + lane) : 0.f;
-      load_features<LI, CPL, LAYOUT>(xn, a.features + xs * A * C, C, c0, active, false);
-      const float* grow = a.gates ? a.gates + e * (int64_t)NP * C : nullptr;
-#pragma unroll
-      for (int p = 0; p < NP; ++p) {
-        if (grow && active) load_vec_stream<CPL>(gn[p], grow + p * C + c0);
-        else {
-#pragma unroll
-          for (int ch = 0; ch < CPL; ++ch) gn[p][ch] = 1.f;
-        }
-      }
     };
-    if (k0 < k1) fetch(k0);
-    for (int64_t k = k0; k < k1; ++k) {
-      float x[A][CPL], g[NP][CPL];
+    // acc += m T_p(x, Y, g) of one path p for one edge (g: the path's gate values).
+    auto path_forward = [&](auto pc, const auto& x, const auto& gp, float m) {
+      constexpr int p = decltype(pc)::value;
+      constexpr int l1 = PS::T.l1[p], l2 = PS::T.l2[p], l3 = PS::T.l3[p];
+      constexpr int m1 = 2 * l1 + 1, m3 = 2 * l3 + 1;
+      constexpr int RO = PS::T.out_row[p], CO = PS::T.coef_off[p];
+      float g[CPL];
 #pragma unroll
-      for (int r = 0; r < A; ++r)
+      for (int ch = 0; ch < CPL; ++ch) g[ch] = gp[ch] * m;
+      float y[2 * l2 + 1];
+      load_harmonics<l2>(y, s_y);
+      static_for<m3>([&](auto kc) {
+        constexpr int kk = decltype(kc)::value;
+        float base[CPL];
 #pragma unroll
-        for (int ch = 0; ch < CPL; ++ch) x[r][ch] = xn[r][ch];
-      const float m = mn;
+        for (int ch = 0; ch < CPL; ++ch) base[ch] = 0.f;
+        static_for<m1>([&](auto ic) {
+          constexpr int i = decltype(ic)::value;
+          if constexpr (BondNonzero<l1, l2, l3, i, kk>::value) {
+            const float b = bond_entry<l1, l2, l3, CO, i, kk>(P.coef, y);
 #pragma unroll
-      for (int p = 0; p < NP; ++p)
-#pragma unroll
-        for (int ch = 0; ch < CPL; ++ch) g[p][ch] = gn[p][ch] * m;
-      if (lane < B) s_y[lane] = yn;
-      if (k + 1 < k1) fetch(k + 1);
-      __syncwarp();
-      static_for<NP>([&](auto pc) {
-        constexpr int p = decltype(pc)::value;
-        constexpr int l1 = PS::T.l1[p], l2 = PS::T.l2[p], l3 = PS::T.l3[p];
-        constexpr int m1 = 2 * l1 + 1, m3 = 2 * l3 + 1;
-        constexpr int RO = PS::T.out_row[p], CO = PS::T.coef_off[p];
-        float y[2 * l2 + 1];
-        load_harmonics<l2>(y, s_y);
-        static_for<m3>([&](auto kc) {
-          constexpr int kk = decltype(kc)::value;
-          float base[CPL];
-#pragma unroll
-          for (int ch = 0; ch < CPL; ++ch) base[ch] = 0.f;
-          static_for<m1>([&](auto ic) {
-            constexpr int i = decltype(ic)::value;
-            if constexpr (BondNonzero<l1, l2, l3, i, kk>::value) {
-              const float b = bond_entry<l1, l2, l3, CO, i, kk>(P.coef, y);
-#pragma unroll
-              for (int ch = 0; ch < CPL; ++ch) base[ch] = fmaf(b, x[l1 * l1 + i][ch], base[ch]);
-            }
-          });
-#pragma unroll
-          for (int ch = 0; ch < CPL; ++ch) acc[RO + kk][ch] = fmaf(base[ch], g[p][ch], acc[RO + kk][ch]);
+            for (int ch = 0; ch < CPL; ++ch) base[ch] = fmaf(b, x[l1 * l1 + i][ch], base[ch]);
+          }
         });
+#pragma unroll
+        for (int ch = 0; ch < CPL; ++ch) acc[RO + kk][ch] = fmaf(base[ch], g[ch], acc[RO + kk][ch]);
       });
-      __syncwarp();
+    };
+
+    if (staged) {
+      bool pending = false;  // the copy of edge k is already in flight
+      for (int64_t k = k0; k < k1; ++k) {
+        const int t = (int)((k - k0) & 31);
+        batch_ids(k, t);
+        const int64_t e = __shfl_sync(0xffffffffu, e_lane, t);
+        const int64_t xs = __shfl_sync(0xffffffffu, s_lane, t);
+        const float m = __shfl_sync(0xffffffffu, m_lane, t);
+        const int slot = (int)(turn & 1u);
+        if (!pending) stage_issue(slot, e, xs);
+        // The other buffer was released by the previous edge: start the next copy.
+        pending = t + 1 < batch;
+        if (pending) {
+          const int64_t en = __shfl_sync(0xffffffffu, e_lane, t + 1);
+          const int64_t sn = __shfl_sync(0xffffffffu, s_lane, t + 1);
+          stage_issue(slot ^ 1, en, sn);
+        }
+        if (lane < B) s_y[lane] = __ldg(a.harmonics + e * B + lane);
+        bool ok = tc::mbar_wait(s_bar + slot, (phases >> slot) & 1u, kStageWaitNs);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) {
+          // Lost copy: record it, give the copies in flight a last bounded chance
+          // to land (the buffers must not be written after the warp leaves), stop.
+          if (lane == 0 && a.status) atomicExch(a.status, 1);
+          tc::mbar_wait(s_bar + slot, (phases >> slot) & 1u, kStageWaitNs);
+          if (pending) tc::mbar_wait(s_bar + (slot ^ 1), (phases >> (slot ^ 1)) & 1u, kStageWaitNs);
+          return;
+        }
+        phases ^= 1u << slot;
+        ++turn;
+        __syncwarp();
+        const float* buf = s_stage + slot * a.stage_floats;
+        float x[A][CPL];
+        load_features_shared<LI, CPL, LAYOUT>(x, buf, C, c0, active);
+        const float* gbuf = buf + A * C;
+        static_for<NP>([&](auto pc) {
+          constexpr int p = decltype(pc)::value;
+          float g[CPL];
+#pragma unroll
+          for (int ch = 0; ch < CPL; ++ch) g[ch] = 1.f;
+          if (a.gates && active) load_vec_shared<CPL>(g, gbuf + p * C + c0);
+          path_forward(pc, x, g, m);
+        });
+        // Every staged value has been consumed (in-order issue): the buffer is free.
+        __syncwarp();
+      }
+    } else if constexpr (CPL == 1) {
+      // Registers of the edge being prefetched.
+      float xn[A][CPL], gn[NP][CPL];
+      float yn = 0.f, mn = 1.f;
+      auto fetch = [&](int64_t k) {
+        const int t = (int)((k - k0) & 31);
+        batch_ids(k, t);
+        const int64_t e = __shfl_sync(0xffffffffu, e_lane, t);
+        const int64_t xs = __shfl_sync(0xffffffffu, s_lane, t);
+        mn = __shfl_sync(0xffffffffu, m_lane, t);
+        yn = lane < B ? __ldg(a.harmonics + e * B + lane) : 0.f;
+        load_features<LI, CPL, LAYOUT>(xn, a.features + xs * A * C, C, c0, active, false);
+        const float* grow = a.gates ? a.gates + e * (int64_t)NP * C : nullptr;
+#pragma unroll
+        for (int p = 0; p < NP; ++p) {
+          if (grow && active) load_vec_stream<CPL>(gn[p], grow + p * C + c0);
+          else {
+#pragma unroll
+            for (int ch = 0; ch < CPL; ++ch) gn[p][ch] = 1.f;
+          }
+        }
+      };
+      if (k0 < k1) fetch(k0);
+      for (int64_t k = k0; k < k1; ++k) {
+        float x[A][CPL], g[NP][CPL];
+#pragma unroll
+        for (int r = 0; r < A; ++r)
+#pragma unroll
+          for (int ch = 0; ch < CPL; ++ch) x[r][ch] = xn[r][ch];
+        const float m = mn;
+#pragma unroll
+        for (int p = 0; p < NP; ++p)
+#pragma unroll
+          for (int ch = 0; ch < CPL; ++ch) g[p][ch] = gn[p][ch];
+        if (lane < B) s_y[lane] = yn;
+        if (k + 1 < k1) fetch(k + 1);
+        __syncwarp();
+        static_for<NP>([&](auto pc) { path_forward(pc, x, g[decltype(pc)::value], m); });
+        __syncwarp();
+      }
     }
     if (active && a.weight) {
       // Path weights are constant over the edges: applied once per output block.

@@ -7,8 +7,10 @@ namespace ictc {
 
 template <int LI, int LE, int LO, int LAYOUT>
 static void add_message(std::vector<Variant>& out) {
-  // The forward keeps a node's whole output row in registers: one channel per lane.
+  // The forward keeps a node's whole output row in registers: one channel per lane,
+  // or two when one warp covers a node (degrees up to 2, staged rows).
   out.push_back(make_variant<LI, LE, LO, 1, LAYOUT, kMessageForward>());
+  if constexpr (LO <= 2) out.push_back(make_variant<LI, LE, LO, 2, LAYOUT, kMessageForward>());
   out.push_back(make_variant<LI, LE, LO, 1, LAYOUT, kMessageAdjoint>());
   out.push_back(make_variant<LI, LE, LO, 2, LAYOUT, kMessageAdjoint>());
 }

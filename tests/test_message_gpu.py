@@ -183,11 +183,11 @@ def test_message_config3_scale_sampled(cuda_device):
     assert torch.isfinite(dx).all()
 
 
-def test_message_adjoint_staged_and_direct_paths_agree(cuda_device):
-    """C64/lmax2 mul_ir (one warp per source node): the adjoint stages each edge's
-    output-gradient row and gate row in shared memory by bulk copy; an output
-    gradient that is not 16-byte aligned takes the direct-load path instead.  Both
-    paths give the same bits, and no staging wait ran out."""
+def test_message_staged_and_direct_paths_agree(cuda_device):
+    """C64/lmax2 mul_ir (one warp per node): the adjoint stages each edge's
+    output-gradient row and gate row in shared memory by bulk copy, the forward each
+    edge's source row and gate row; operands that are not 16-byte aligned take the
+    direct-load kernels instead.  Both paths agree, and no staging wait ran out."""
     from ictc_o3.backends.cuda.message import packed_graph_message
     from ictc_o3.backends.cuda.tensor_product import get_plan
     C, L, nodes, edges = 64, 2, 300, 5000
@@ -210,4 +210,12 @@ def test_message_adjoint_staged_and_direct_paths_agree(cuda_device):
     direct = torch.autograd.grad(out, [x, y, gates], shifted)
     for a, b in zip(staged, direct):
         assert torch.equal(a, b)
+    # Forward: 16-byte aligned rows take the staged two-channels-per-lane kernel,
+    # a shifted feature buffer the one-channel-per-lane kernel with direct loads.
+    xs = torch.empty(x.numel() + 1, device=cuda_device)[1:].view_as(x)
+    xs.copy_(x.detach())
+    assert xs.data_ptr() % 16 != 0
+    with torch.no_grad():
+        out_direct = packed_graph_message(owner, "mul_ir", xs, y.detach(), gates.detach(), src, dst, mask)
+    torch.testing.assert_close(out_direct, out.detach(), rtol=1e-6, atol=1e-6)
     assert get_plan(owner, "mul_ir", cuda_device).status() == 0
