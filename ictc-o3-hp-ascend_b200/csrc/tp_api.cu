@@ -38,6 +38,8 @@ struct ictc_tp_plan {
   int cpl[kKinds], slices[kKinds], block[kKinds], grid[kKinds];
   size_t smem[kKinds];
   int stage_floats;         // graph adjoint staging buffer per warp (0 = not staged)
+  size_t adj_staged_smem;
+  int adj_staged_grid;
   // Staged graph forward, two channels per lane (one warp per node), used when
   // the feature and gate rows of a launch are 16-byte aligned; else v[kMessageForward].
   const Variant* fwd2;
@@ -173,10 +175,11 @@ extern "C" int ictc_tp_plan_create(int channels, int input_lmax, int edge_lmax, 
   {
     const Variant* va = plan->v[kMessageAdjoint];
     const int stage = (va->rows + va->np) * channels;
-    const bool fits = plan->slices[kMessageAdjoint] == 1 && (va->rows * channels) % 4 == 0 &&
+    const bool fits = va->fn_staged && plan->slices[kMessageAdjoint] == 1 && (va->rows * channels) % 4 == 0 &&
                       (va->np * channels) % 4 == 0 && stage * 4 <= kStageBudgetBytes;
     plan->stage_floats = fits ? stage : 0;
-    if (fits) plan->smem[kMessageAdjoint] = staged_smem_bytes((int)va->smem, stage);
+    plan->adj_staged_smem = fits ? staged_smem_bytes((int)va->smem, stage) : 0;
+    plan->adj_staged_grid = 0;
   }
   plan->fwd2 = nullptr;
   plan->fwd2_stage_floats = plan->fwd2_grid = 0;
@@ -216,6 +219,14 @@ extern "C" int ictc_tp_plan_create(int channels, int input_lmax, int edge_lmax, 
     cudaFuncSetAttribute(v->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan->smem[kind]);
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v->fn, plan->block[kind], plan->smem[kind]);
     plan->grid[kind] = sms * (per_sm < 1 ? 1 : per_sm);
+  }
+  if (plan->stage_floats > 0) {
+    const Variant* va = plan->v[kMessageAdjoint];
+    int per_sm = 0;
+    cudaFuncSetAttribute(va->fn_staged, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan->adj_staged_smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, va->fn_staged, plan->block[kMessageAdjoint],
+                                                  plan->adj_staged_smem);
+    plan->adj_staged_grid = sms * (per_sm < 1 ? 1 : per_sm);
   }
   if (plan->fwd2) {
     int per_sm = 0;
@@ -294,15 +305,20 @@ static int launch(const ictc_tp_plan* plan, int kind, TPArgs& args, int64_t unit
     args.slices = 1;
     args.stage_floats = plan->fwd2_stage_floats;
   }
+  Launcher launcher = v->launch;
   if (kind == kMessageAdjoint && plan->stage_floats > 0 &&
       (reinterpret_cast<uintptr_t>(args.grad_out) & 15u) == 0 &&
-      (reinterpret_cast<uintptr_t>(args.gates) & 15u) == 0)
+      (reinterpret_cast<uintptr_t>(args.gates) & 15u) == 0) {
     args.stage_floats = plan->stage_floats;
+    launcher = v->launch_staged;
+    grid_cap = plan->adj_staged_grid;
+    smem = plan->adj_staged_smem;
+  }
   if (args.rows <= 0) return ICTC_OK;
   int64_t work = (args.rows * (kind == kAdjoint || kind == kMessageAdjoint ? 1 : args.slices) + units_per_block - 1) /
                  units_per_block;
   int grid = (int)(work < grid_cap ? work : grid_cap);
-  cudaError_t err = v->launch(args, plan->coef.data(), grid, plan->block[kind], smem, (cudaStream_t)stream);
+  cudaError_t err = launcher(args, plan->coef.data(), grid, plan->block[kind], smem, (cudaStream_t)stream);
   if (err != cudaSuccess) {
     ictc_set_error(what, cudaGetErrorString(err));
     return ICTC_ERR_CUDA;

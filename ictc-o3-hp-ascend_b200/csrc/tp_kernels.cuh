@@ -412,8 +412,9 @@ __global__ void __launch_bounds__(kThreads, (LO >= 3) ? 1 : 2)
 // that walks the same edges; their dY partials meet in shared memory behind a
 // named barrier of the group (deterministic, no global atomics).
 // ---------------------------------------------------------------------------
-template <int LI, int LE, int LO, int CPL, int LAYOUT, bool GRAPH>
-__global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoint_kernel(const __grid_constant__ CoefParams<Paths<LI, LE, LO>::CT> P) {
+template <int LI, int LE, int LO, int CPL, int LAYOUT, bool GRAPH, bool STAGED = false>
+__global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2)
+    tp_adjoint_kernel(const __grid_constant__ CoefParams<Paths<LI, LE, LO>::CT> P) {
   using PS = Paths<LI, LE, LO>;
   constexpr int A = PS::A, B = PS::B;
   const TPArgs& a = P.a;
@@ -556,7 +557,14 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
   // Graph adjoint staging (one warp per node): each edge's output-gradient row and
   // gate row arrive in this warp's shared buffer by bulk copy, completed on its
   // mbarrier; the copy of the next edge is issued as soon as the buffer is free.
-  const bool staged = GRAPH && a.stage_floats > 0;
+  constexpr bool staged = GRAPH && STAGED;
+  if constexpr (staged) {
+    // Launched only with a staging buffer (one warp per node, aligned rows).
+    if (a.stage_floats <= 0 || a.slices != 1) {
+      if (threadIdx.x == 0 && a.status) atomicExch(a.status, 2);
+      return;
+    }
+  }
   uint64_t* s_bar = nullptr;
   float* s_stage = nullptr;
   uint32_t phase = 0;
@@ -642,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
         const int64_t e = __shfl_sync(0xffffffffu, e_lane, t);
         const int64_t d = __shfl_sync(0xffffffffu, d_lane, t);
         const float m = __shfl_sync(0xffffffffu, m_lane, t);
-        if (staged) {
+        if constexpr (staged) {
           if (!pending) stage_issue(e, d);
           bool ok = tc::mbar_wait(s_bar, phase, kStageWaitNs);
           ok = __all_sync(0xffffffffu, ok);
@@ -677,7 +685,7 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2) tp_adjoi
 #pragma unroll
         for (int j = 0; j < B; ++j) dyp[j] = 0.f;
         float* dgrow = want_dg ? a.grad_gates + e * (int64_t)PS::NP * C : nullptr;
-        if (staged) {
+        if constexpr (staged) {
           const float* grow = a.gates ? s_stage + PS::ROWS * C : nullptr;
           static_for<PS::NP>([&](auto pc) {
             constexpr int l1 = PS::T.l1[decltype(pc)::value];
@@ -721,6 +729,8 @@ struct Variant {
   int li, le, lo, cpl, layout, kind;
   const void* fn;       // kernel symbol (occupancy queries)
   Launcher launch;
+  const void* fn_staged;  // graph adjoint with staged rows (null for other kinds)
+  Launcher launch_staged;
   int np, bond_width, coef_total, rows, a, b;
   size_t smem;
 };
@@ -741,7 +751,7 @@ cudaError_t launch_plain(const TPArgs& args, const float*, int grid, int block, 
 }
 
 // Kernels that read the CG table from the parameter bank get it by value.
-template <int LI, int LE, int LO, int CPL, int LAYOUT, int KIND>
+template <int LI, int LE, int LO, int CPL, int LAYOUT, int KIND, bool STAGED = false>
 cudaError_t launch_coef(const TPArgs& args, const float* coef, int grid, int block, size_t smem,
                         cudaStream_t stream) {
   using PS = Paths<LI, LE, LO>;
@@ -751,7 +761,7 @@ cudaError_t launch_coef(const TPArgs& args, const float* coef, int grid, int blo
   if constexpr (KIND == kMessageForward)
     tp_message_forward_kernel<LI, LE, LO, CPL, LAYOUT><<<grid, block, smem, stream>>>(params);
   else
-    tp_adjoint_kernel<LI, LE, LO, CPL, LAYOUT, KIND == kMessageAdjoint><<<grid, block, smem, stream>>>(params);
+    tp_adjoint_kernel<LI, LE, LO, CPL, LAYOUT, KIND == kMessageAdjoint, STAGED><<<grid, block, smem, stream>>>(params);
   return cudaGetLastError();
 }
 
@@ -759,6 +769,8 @@ template <int LI, int LE, int LO, int CPL, int LAYOUT, int KIND>
 Variant make_variant() {
   using PS = Paths<LI, LE, LO>;
   Variant v = describe<PS>(CPL, LAYOUT, KIND, LI, LE, LO);
+  v.fn_staged = nullptr;
+  v.launch_staged = nullptr;
   if constexpr (KIND == kForward) {
     v.fn = (const void*)tp_forward_kernel<LI, LE, LO, CPL, LAYOUT>;
     v.launch = launch_plain<LI, LE, LO, CPL, LAYOUT, KIND>;
@@ -768,6 +780,10 @@ Variant make_variant() {
   } else {
     v.fn = (const void*)tp_adjoint_kernel<LI, LE, LO, CPL, LAYOUT, KIND == kMessageAdjoint>;
     v.launch = launch_coef<LI, LE, LO, CPL, LAYOUT, KIND>;
+    if constexpr (KIND == kMessageAdjoint && LO <= 2) {
+      v.fn_staged = (const void*)tp_adjoint_kernel<LI, LE, LO, CPL, LAYOUT, true, true>;
+      v.launch_staged = launch_coef<LI, LE, LO, CPL, LAYOUT, KIND, true>;
+    }
   }
   return v;
 }
