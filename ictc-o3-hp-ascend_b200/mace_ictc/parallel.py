@@ -230,9 +230,14 @@ def distributed_energy_forces(model, layout: SlabLayout, pos_local: torch.Tensor
     total = energy.detach().reshape(1)
     w = None
     if virial:
-        tensor = -(vec.detach().t() @ g)
-        tensor = 0.5 * (tensor + tensor.t())
-        w = torch.stack([tensor[0, 0], tensor[1, 1], tensor[2, 2], tensor[0, 1], tensor[0, 2], tensor[1, 2]])
+        # -sum_e r_e (x) g_e, symmetrised, as three column-product reductions over the
+        # edges (a 3 x E by E x 3 matrix product is a poorly shaped GEMM for E ~ 1e7).
+        r = vec.detach()
+        diag = (r * g).sum(0)                                  # r_x g_x, r_y g_y, r_z g_z
+        up = (r * g[:, [1, 2, 0]]).sum(0)                      # r_x g_y, r_y g_z, r_z g_x
+        down = (r * g[:, [2, 0, 1]]).sum(0)                    # r_x g_z, r_y g_x, r_z g_y
+        w = -torch.stack([diag[0], diag[1], diag[2], 0.5 * (up[0] + down[1]), 0.5 * (down[0] + up[2]),
+                          0.5 * (up[1] + down[2])])
     if layout.world > 1:
         dist.all_reduce(total)
         if w is not None:
