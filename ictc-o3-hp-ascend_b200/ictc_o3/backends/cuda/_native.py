@@ -43,6 +43,8 @@ _SIGNATURES = {
     "ictc_neighbor_noalloc_scratch_bytes": [],
     "ictc_neighbor_list_noalloc": [_p, _i64, _p, ctypes.c_float, _p, _p, _p, _p, _i64, _p],
     "ictc_direction_harmonics": [_p, _p, _p, _p, _p, _p, _i64, _i, _i, _p],
+    "ictc_edge_geometry": [_p, _i64, ctypes.c_float, _i, _i, _i, _p, _p, _p, _p],
+    "ictc_edge_geometry_backward": [_p, _p, _p, _i64, ctypes.c_float, _i, _i, _i, _p, _p],
     "ictc_channel_mix_tile_nodes": [],
     "ictc_channel_mix": [_p, _i64, _i64, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i, _i, _i, ctypes.c_float, _i,
                          _p],

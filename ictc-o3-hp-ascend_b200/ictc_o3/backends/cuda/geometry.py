@@ -91,3 +91,77 @@ def direction_harmonics(n: torch.Tensor, lmax: int) -> torch.Tensor:
     else:
         y = _launch(flat, int(lmax), 0)[0]
     return y.reshape(*lead, (lmax + 1) ** 2)
+
+
+# ---------------------------------------------------------------------------
+# Edge geometry: unit vectors, Bessel x polynomial-envelope embedding, cutoff mask
+# ---------------------------------------------------------------------------
+
+def edge_geometry_reference(vec, r_max, num_basis, p, basis_norm=True):
+    """The same map in torch ops (mace_ictc/models/radial_basis.py:11-91 and the
+    model's edge normalisation); differentiable to any order."""
+    import math
+    r = vec.norm(dim=-1)
+    unit = vec / r.clamp_min(1e-8).unsqueeze(-1)
+    x = r / r_max
+    env = (1.0 - ((p + 1.0) * (p + 2.0) / 2.0) * x.pow(p) + p * (p + 2.0) * x.pow(p + 1)
+           - (p * (p + 1.0) / 2.0) * x.pow(p + 2)) * (r < r_max).to(vec.dtype)
+    freq = math.pi / r_max * torch.arange(1, num_basis + 1, dtype=vec.dtype, device=vec.device)
+    radial = math.sqrt(2.0 / r_max) * torch.sin(r.unsqueeze(-1) * freq) / r.clamp_min(1e-12).unsqueeze(-1)
+    radial = radial * env.unsqueeze(-1)
+    if basis_norm:
+        radial = radial * math.sqrt(num_basis)
+    mask = (r <= r_max).to(vec.dtype)
+    return unit, radial, mask
+
+
+def _geometry_args(r_max, num_basis, p, basis_norm):
+    return float(r_max), int(num_basis), int(p), int(bool(basis_norm))
+
+
+class _EdgeGeometry(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, vec, r_max, num_basis, p, basis_norm):
+        ctx.args = (r_max, num_basis, p, basis_norm)
+        ctx.save_for_backward(vec)
+        edges = vec.shape[0]
+        unit = torch.empty(edges, 3, device=vec.device, dtype=torch.float32)
+        radial = torch.empty(edges, num_basis, device=vec.device, dtype=torch.float32)
+        mask = torch.empty(edges, device=vec.device, dtype=torch.float32)
+        if edges:
+            _native.call("ictc_edge_geometry", ptr(vec), int(edges), *_geometry_args(r_max, num_basis, p, basis_norm),
+                         ptr(unit), ptr(radial), ptr(mask), stream_of(vec))
+        ctx.mark_non_differentiable(mask)
+        return unit, radial, mask
+
+    @staticmethod
+    def backward(ctx, g_unit, g_radial, _g_mask):
+        (vec,) = ctx.saved_tensors
+        if not required_gradients((vec,), ctx.needs_input_grad[:1])[0]:
+            return None, None, None, None, None
+        if torch.is_grad_enabled():
+            # The gradient itself is differentiated (force-loss training): recompute
+            # through the torch formula so every order is available.
+            with torch.enable_grad():
+                unit, radial, _ = edge_geometry_reference(vec, *ctx.args)
+                outs, grads = [], []
+                for o, g in ((unit, g_unit), (radial, g_radial)):
+                    if g is not None:
+                        outs.append(o)
+                        grads.append(g)
+                (dv,) = torch.autograd.grad(outs, [vec], grads, create_graph=True)
+            return dv, None, None, None, None
+        grad_vec = torch.empty_like(vec)
+        if vec.shape[0]:
+            _native.call("ictc_edge_geometry_backward", ptr(vec),
+                         ptr(None if g_unit is None else g_unit.contiguous()),
+                         ptr(None if g_radial is None else g_radial.contiguous()), int(vec.shape[0]),
+                         *_geometry_args(*ctx.args), ptr(grad_vec), stream_of(vec))
+        return grad_vec, None, None, None, None
+
+
+def edge_geometry(vec: torch.Tensor, r_max: float, num_basis: int, p: int, basis_norm: bool = True):
+    """(unit [E, 3], radial [E, num_basis], mask [E]) of CUDA FP32 edge vectors [E, 3]."""
+    if vec.dtype != torch.float32 or vec.device.type != "cuda" or vec.dim() != 2 or vec.shape[1] != 3:
+        raise ValueError("edge geometry requires CUDA FP32 edge vectors [E, 3]")
+    return _EdgeGeometry.apply(vec.contiguous(), float(r_max), int(num_basis), int(p), bool(basis_norm))

@@ -43,6 +43,11 @@ class CudaOps:
         from ictc_o3.backends.cuda.geometry import direction_harmonics
         return direction_harmonics(n, lmax)
 
+    def edge_geometry(self, vec, r_max, num_basis, p):
+        """(unit vectors, radial embedding, cutoff mask): one fused kernel each way."""
+        from ictc_o3.backends.cuda.geometry import edge_geometry
+        return edge_geometry(vec, r_max, num_basis, p)
+
     def message(self, tp, features, harmonics, gates, src, dst, mask, dst_nodes):
         from ictc_o3.backends.cuda.message import packed_graph_message
         return packed_graph_message(tp, "mul_ir", features, harmonics, gates, src, dst, mask, dst_nodes)
@@ -278,11 +283,15 @@ class MACEICTC(nn.Module):
 
     def edge_features(self, vec):
         """Harmonics, radial embedding and cutoff mask of edge vectors r_e = pos[dst] - pos[src] + shift."""
-        length = vec.norm(dim=1)
-        n = vec / length.clamp_min(1e-8).unsqueeze(-1)
+        geometry = getattr(self.ops, "edge_geometry", None)
+        if geometry is not None:
+            n, feats, mask = geometry(vec, self.r_max, self.num_basis, self.p)
+        else:
+            length = vec.norm(dim=1)
+            n = vec / length.clamp_min(1e-8).unsqueeze(-1)
+            feats = radial_embedding(length, self.r_max, self.num_basis, self.p)
+            mask = (length <= self.r_max).to(vec.dtype).detach()
         harmonics = self.ops.harmonics(n, self.lmax)
-        feats = radial_embedding(length, self.r_max, self.num_basis, self.p)
-        mask = (length <= self.r_max).to(vec.dtype).detach()
         return harmonics, feats, mask
 
     def edge_inputs(self, pos, src, dst, shift_vectors):

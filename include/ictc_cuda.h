@@ -156,6 +156,22 @@ int ictc_direction_harmonics(const float* directions, const float* table, const 
                              int mode, void* stream);
 
 /*
+ * Edge geometry of one interaction, fused: for edge vectors vec [E, 3],
+ *   unit = vec / max(|vec|, 1e-8)  [E, 3],  mask = (|vec| <= r_max)  [E],
+ *   radial [E, num_basis] = Bessel basis sqrt(2/r_max) sin(b pi r / r_max) / r
+ *                           x polynomial envelope of order p (x sqrt(num_basis) if basis_norm).
+ * Replaces the elementwise chain of mace_ictc/models/radial_basis.py:11-39
+ * (mace_polynomial_cutoff) and :42-91 (mace_radial_embedding, Bessel kind) with the
+ * edge normalisation of the interaction's edge features.  num_basis <= 16, p >= 1.
+ * The backward maps grad_unit [E, 3] and grad_radial [E, num_basis] (either may be
+ * NULL) to grad_vec [E, 3].
+ */
+int ictc_edge_geometry(const float* vec, int64_t edges, float r_max, int num_basis, int p, int basis_norm,
+                       float* unit, float* radial, float* mask, void* stream);
+int ictc_edge_geometry_backward(const float* vec, const float* grad_unit, const float* grad_radial, int64_t edges,
+                                float r_max, int num_basis, int p, int basis_norm, float* grad_vec, void* stream);
+
+/*
  * MACE symmetric contraction as a per-node polynomial (correlation 1..3,
  * input degrees 0..lmax with 1 <= lmax <= 3, targets 0..target_lmax <= lmax).
  *   x      [N, C*(lmax+1)^2]   node features, degree blocks [C][2l+1] (mul_ir)
