@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the ICTC-O3 hot path on B200: the C128/lmax-3 channelwise tensor product.
 
-Workload: FP32 path-preserving TP, C=128, lmax 3 (23 paths),
+Workload (benchmark configs[1]): FP32 path-preserving TP, C=128, lmax 3 (23 paths),
 262,144 instances per forward step; forward+VJP (grads of features, harmonics and
 per-instance path weights) at 131,072 instances per step.  Inputs are seeded
 synthetic tensors with the config's distributions: features N(0,1), harmonics of
@@ -57,6 +57,8 @@ def parse_args():
                    help="atoms of the --profile-block (default 16,384) or --profile-md (default 262,144) system")
     p.add_argument("--profile-md", action="store_true",
                    help="time only the configs[4] MD step (torchrun for several GPUs)")
+    p.add_argument("--phases", action="store_true",
+                   help="with --profile-md: per-phase CUDA-event breakdown of the step (max over ranks)")
     p.add_argument("--profile-train", action="store_true", help="time only the configs[3] training step")
     p.add_argument("--profile-radial", action="store_true",
                    help="time only the fused radial MLP kernels (forward, backward) at --rows edges, --gates columns")
@@ -254,7 +256,7 @@ def e2e_forward(op, rows, steps, warmup, device, world):
 
 
 def mace_block(device, steps, warmup, atoms=16384, cpu_seconds=0.0):
-    """BASELINE configs[2]: one non-first MACE interaction block (input lmax 2) and its product
+    """configs[2]: one non-first MACE interaction block (input lmax 2) and its product
     block, C64/lmax2, correlation 3, 16,384 H/C/O atoms at 0.1/A^3 (5 A cutoff), forward plus
     the force gradient.  Returns the JSON sub-object."""
     from ictc_o3.backends.cuda.neighbors import neighbor_list
@@ -335,7 +337,7 @@ def mace_block_cpu(seconds, atoms=1024):
 
 
 def mace_train(device, steps, warmup, configs=4, atoms=2048, cutoff=5.0):
-    """BASELINE configs[3]: force-loss training step of MACE C128/lmax3, 2 interactions,
+    """configs[3]: force-loss training step of MACE C128/lmax3, 2 interactions,
     correlation 3.  A batch of 4 periodic configurations of 2,048 H/C/O atoms (0.1/A^3,
     minimum distance 0.9 A); synthetic targets: per-atom energy N(0,1) and forces N(0,1).
     loss = mean_c (E_c/N_c - e_c)^2 + 100 mean (F - F_t)^2; each step runs forward, forces
@@ -387,47 +389,61 @@ def mace_train(device, steps, warmup, configs=4, atoms=2048, cutoff=5.0):
                         "loss = E MSE (per atom) + 100 x F MSE, backward through mixed second derivatives, Adam"}
 
 
-def mace_md(device, world, rank, steps, warmup, atoms=262144, cutoff=5.0):
-    """BASELINE configs[4]: MACE energy + forces + virial MD step, C64/lmax2, 2 interactions,
+def mace_md(device, world, rank, steps, warmup, atoms=262144, cutoff=5.0, phases=False):
+    """configs[4]: MACE energy + forces + virial MD step, C64/lmax2, 2 interactions,
     correlation 3, 262,144 H/C/O atoms at 0.1/A^3, slab-partitioned along x over the ranks
-    with one-cutoff halos.  Every step rebuilds the slab layout and the neighbour lists, then
-    runs the model with the feature halo exchange after layer 1 (and its adjoint) and returns
-    ghost forces to their owners.  Strong scaling: the system size is fixed.
+    with one-cutoff halos.  Each rank holds only its own atoms (distributed once, before
+    timing).  Every step migrates atoms between slabs, exchanges ghost positions, rebuilds
+    the neighbour list, runs the model with the feature halo exchange before layer 2 (and
+    its adjoint) and returns ghost forces to their owners.  Strong scaling: the system
+    size is fixed.
 
-    ``value`` times device-resident positions; ``e2e`` adds, every step, the H2D copy of the
-    positions from pinned host memory and the D2H read of the owned forces, energy and virial."""
+    ``value`` times device-resident positions; ``e2e`` adds, every step, the H2D copy of
+    each rank's owned positions from pinned host memory and the D2H read of the owned
+    forces, energy and virial.  ``phases`` adds a per-phase breakdown (CUDA events on the
+    compute stream and host time between marks, median over the timed steps, max over
+    ranks)."""
     from mace_ictc.models import MACEICTC
-    from mace_ictc.parallel import distributed_energy_forces, local_positions, slab_edges, slab_layout
+    from mace_ictc.parallel import StepPhases, md_step, partition
     from mace_ictc.systems import random_system
     side = (atoms / 0.1) ** (1.0 / 3.0)
-    if rank == 0:
-        pos, species, side0 = random_system(atoms, seed=41, device=device)
-        assert abs(side0 - side) < 1e-9
-    else:
-        pos = torch.empty(atoms, 3, device=device)
-        species = torch.empty(atoms, dtype=torch.int64, device=device)
-    if world > 1:
-        torch.distributed.broadcast(pos, 0)
-        torch.distributed.broadcast(species, 0)
+    pos, species, side0 = random_system(atoms, seed=41, device=device)   # same seed on every rank
+    assert abs(side0 - side) < 1e-9
+    domain = partition(pos, species, side, rank, world, cutoff)
+    del pos, species
     torch.manual_seed(0)
     model = MACEICTC(channels=64, lmax=2, num_interactions=2, correlation=3, r_max=cutoff,
                      avg_num_neighbors=52.0).to(device)
     torch.cuda.reset_peak_memory_stats(device)
     stats = {}
+    state = {"domain": domain}
+    recorder = StepPhases(enabled=phases)
+    tables = []
 
-    def step(positions):
-        layout = slab_layout(positions, side, rank, world, cutoff)
-        p = local_positions(layout, positions, side)
-        src, dst, shift = slab_edges(layout, p, side, cutoff, cutoff)
-        stats.update(owned=layout.owned, ghosts=layout.local - layout.owned, edges=int(src.numel()))
-        return distributed_energy_forces(model, layout, p, species.index_select(0, layout.local_global),
-                                         src, dst, shift)
+    def step():
+        recorder.reset()
+        d, energy, forces, virial = md_step(model, state["domain"], cutoff, phases=recorder)
+        state["domain"] = d
+        if phases:
+            tables.append(recorder.summary())
+        return energy, forces, virial
 
-    ms = time_loop(lambda: step(pos), steps, warmup, world, device) / steps
+    ms = time_loop(step, steps, warmup, world, device) / steps
     ms = max_over_ranks(ms, world, device)
+    result_phases = None
+    if phases:
+        names = [name for name, _, _ in tables[-1]]
+        med = torch.tensor([[statistics.median(t[i][1] for t in tables[warmup:]),
+                             statistics.median(t[i][2] for t in tables[warmup:])] for i in range(len(names))],
+                           device=device, dtype=torch.float64)
+        if world > 1:
+            torch.distributed.all_reduce(med, op=torch.distributed.ReduceOp.MAX)
+        result_phases = {name: {"device_ms": round(float(med[i, 0]), 3), "host_ms": round(float(med[i, 1]), 3)}
+                         for i, name in enumerate(names)}
+        recorder.enabled = False
 
-    pos_host = pos.cpu().pin_memory()
-    pos_dev = torch.empty_like(pos)
+    owned_host = state["domain"].pos.cpu().pin_memory()
+    pos_dev = torch.empty_like(state["domain"].pos)
     out_host = {}
 
     def pinned(name, t):
@@ -437,26 +453,37 @@ def mace_md(device, world, rank, steps, warmup, atoms=262144, cutoff=5.0):
         return buf
 
     def e2e_step():
-        pos_dev.copy_(pos_host, non_blocking=True)
-        energy, forces, virial = step(pos_dev)
+        pos_dev.copy_(owned_host, non_blocking=True)
+        d = state["domain"]
+        d.pos = pos_dev
+        d, energy, forces, virial = md_step(model, d, cutoff)
+        state["domain"] = d
         pinned("forces", forces).copy_(forces, non_blocking=True)
         ev = torch.cat([energy, virial])
         pinned("ev", ev).copy_(ev, non_blocking=True)
+        stats.update(owned=d.owned, forces=forces.shape[0])
 
     e2e_steps = max(2, steps)
     e2e_ms = time_loop(e2e_step, e2e_steps, 1, world, device) / e2e_steps
     e2e_ms = max_over_ranks(e2e_ms, world, device)
     peak_gb = max_over_ranks(torch.cuda.max_memory_allocated(device) / 1e9, world, device)
-    ghost_rows = stats["ghosts"]
-    return {"value": round(atoms / (ms * 1e-3), 1), "unit": "atom-steps/s", "ms_per_step": round(ms, 2),
-            "n_gpus": world, "scaling": "strong", "atoms": atoms,
-            "per_rank_rank0": {"owned": stats["owned"], "ghosts": ghost_rows, "edges": stats["edges"]},
-            "halo_bytes_per_exchange_rank0": ghost_rows * 64 * 9 * 4,
-            "peak_device_gb": round(peak_gb, 1),
-            "workload": "configs[4]: MACE C64/lmax2, 2 interactions, corr 3, E+F+virial, neighbour rebuild "
-                        "every step, slab partition along x with 5 A halos, NCCL P2P feature exchange",
-            "e2e": {"value": round(atoms / (e2e_ms * 1e-3), 1), "unit": "atom-steps/s",
-                    "h2d_bytes_per_step": atoms * 12, "d2h_bytes_per_step": stats["owned"] * 12 + 28}}
+    from mace_ictc.parallel import halo_layout, slab_edges
+    layout, p, _ = halo_layout(state["domain"])
+    src, _, _ = slab_edges(layout, p, cutoff)
+    ghost_rows = layout.local - layout.owned
+    result = {"value": round(atoms / (ms * 1e-3), 1), "unit": "atom-steps/s", "ms_per_step": round(ms, 2),
+              "n_gpus": world, "scaling": "strong", "atoms": atoms,
+              "per_rank_rank0": {"owned": layout.owned, "ghosts": ghost_rows, "edges": int(src.numel())},
+              "halo_bytes_per_exchange_rank0": ghost_rows * 64 * 9 * 4,
+              "peak_device_gb": round(peak_gb, 1),
+              "workload": "configs[4]: MACE C64/lmax2, 2 interactions, corr 3, E+F+virial, migration, ghost "
+                          "positions and neighbour rebuild every step, slab partition along x with 5 A halos, "
+                          "NCCL P2P feature exchange",
+              "e2e": {"value": round(atoms / (e2e_ms * 1e-3), 1), "unit": "atom-steps/s",
+                      "h2d_bytes_per_step": atoms * 12, "d2h_bytes_per_step": atoms * 12 + world * 28}}
+    if result_phases is not None:
+        result["phases"] = result_phases
+    return result
 
 
 def run_ours(args):
@@ -676,7 +703,7 @@ def main():
         torch.cuda.set_device(device)
         from ictc_o3.backends.cuda import _native
         _native.library()
-        md = mace_md(device, world, rank, args.steps, args.warmup, atoms=args.atoms or 262144)
+        md = mace_md(device, world, rank, args.steps, args.warmup, atoms=args.atoms or 262144, phases=args.phases)
         if rank == 0:
             print(json.dumps({"profile_md": md}), flush=True)
         if world > 1:

@@ -165,3 +165,22 @@ def edge_geometry(vec: torch.Tensor, r_max: float, num_basis: int, p: int, basis
     if vec.dtype != torch.float32 or vec.device.type != "cuda" or vec.dim() != 2 or vec.shape[1] != 3:
         raise ValueError("edge geometry requires CUDA FP32 edge vectors [E, 3]")
     return _EdgeGeometry.apply(vec.contiguous(), float(r_max), int(num_basis), int(p), bool(basis_norm))
+
+
+def edge_vectors(positions: torch.Tensor, cell: torch.Tensor, shifts: torch.Tensor, batch: torch.Tensor,
+                 source: torch.Tensor, destination: torch.Tensor) -> torch.Tensor:
+    """r_e = pos[dst] - pos[src] + shifts_e @ cell[batch[src]]  (``backends/ascend/geometry.py:6``,
+    hook site ``pure_cartesian_ictd_fix.py:2926-2928``).
+
+    ``shifts`` are lattice coordinates [E, 3] and ``cell`` is [B, 3, 3].  Device
+    gathers and a batched 3 x 3 product that autograd differentiates to any order
+    in positions and cell (strain derivatives stay live)."""
+    if any(t.dtype != torch.float32 or t.device.type != "cuda" for t in (positions, cell, shifts)):
+        raise ValueError("edge_vectors requires CUDA FP32 positions, cell and shifts")
+    if cell.ndim != 3 or cell.shape[1:] != (3, 3) or shifts.shape != (source.numel(), 3):
+        raise ValueError("Expected cell [B,3,3] and lattice shifts [E,3]")
+    if cell.shape[0] == 1:
+        shift_vectors = shifts @ cell[0]
+    else:
+        shift_vectors = torch.bmm(shifts.unsqueeze(1), cell.index_select(0, batch.index_select(0, source))).squeeze(1)
+    return positions.index_select(0, destination) - positions.index_select(0, source) + shift_vectors

@@ -25,51 +25,51 @@ def tile_nodes() -> int:
     return int(_native.library().ictc_channel_mix_tile_nodes())
 
 
-def species_layout(species: torch.Tensor, num_elements: int):
-    """(order, counts): nodes sorted by species (stable) and the node count of each
-    species, with a single device-to-host read; cached on the tensor's identity and
-    version and shared by every per-species structure built from it."""
+def check_species(species: torch.Tensor, num_elements: int):
+    """Raise if a species index is outside [0, num_elements) (``backends/ascend/species.py:9-17``).
+    One device-to-host read per (tensor, version); later calls on the same tensor are free."""
     key = (species._version, int(num_elements))
-    cached = getattr(species, "_ictc_species_layout", None)
-    if cached is not None and cached[0] == key:
-        return cached[1]
-    index = species.to(torch.int64)
-    order = torch.argsort(index, stable=True)
-    sorted_species = index.index_select(0, order)
-    bounds = torch.arange(num_elements + 1, dtype=torch.int64, device=species.device)
-    edges = torch.searchsorted(sorted_species, bounds)
-    if index.numel():
-        probe = torch.cat([edges, sorted_species[:1], sorted_species[-1:]]).cpu().tolist()
-        edges_h, lo, hi = probe[:-2], probe[-2], probe[-1]
+    if getattr(species, "_ictc_species_checked", None) == key:
+        return
+    if species.numel():
+        lo, hi = torch.stack([species.amin(), species.amax()]).cpu().tolist()
         if lo < 0 or hi >= num_elements:
             raise ValueError("Species index is outside the element table")
-    else:
-        edges_h = [0] * (num_elements + 1)
-    counts = [edges_h[s + 1] - edges_h[s] for s in range(num_elements)]
-    result = (order, counts)
     try:
-        species._ictc_species_layout = (key, result)
+        species._ictc_species_checked = key
     except AttributeError:
         pass
-    return result
 
 
 def species_tiles_of(species: torch.Tensor, num_elements: int, nb: int):
-    """Species-homogeneous node tiles [T, nb] (-1 padded) and their species [T] (int32)."""
-    order, counts = species_layout(species, num_elements)
-    tiles, tspecies, start = [], [], 0
-    for s, count in enumerate(counts):
-        if count:
-            padded = -(-count // nb) * nb
-            block = torch.full((padded,), -1, dtype=torch.int64, device=species.device)
-            block[:count] = order[start:start + count]
-            tiles.append(block.view(-1, nb))
-            tspecies.append(torch.full((padded // nb,), s, dtype=torch.int32, device=species.device))
-        start += count
-    if tiles:
-        return torch.cat(tiles).contiguous(), torch.cat(tspecies).contiguous()
-    return (torch.empty(0, nb, dtype=torch.int64, device=species.device),
-            torch.empty(0, dtype=torch.int32, device=species.device))
+    """Species-homogeneous node tiles [T, nb] (-1 padded) and their species [T] (int32).
+
+    Built on the device without a host read: nodes sorted by species (stable), each
+    species' run cut into tiles of nb nodes, the last one padded with -1.  T is the
+    bound nodes // nb + num_elements; tiles past the used ones hold only -1 nodes,
+    which the kernels skip."""
+    check_species(species, num_elements)
+    device = species.device
+    n, S = species.numel(), int(num_elements)
+    T = n // nb + S
+    index = species.to(torch.int64)
+    order = torch.argsort(index, stable=True)
+    bounds = torch.searchsorted(index.index_select(0, order), torch.arange(S + 1, dtype=torch.int64, device=device))
+    counts = bounds[1:] - bounds[:-1]
+    tiles_per = (counts + nb - 1) // nb
+    tile_end = torch.cumsum(tiles_per, 0)
+    t = torch.arange(T, dtype=torch.int64, device=device)
+    s = torch.searchsorted(tile_end, t, right=True)                 # species of tile t (S: unused tile)
+    used = s < S
+    s = torch.clamp(s, max=S - 1)
+    j = t - (tile_end - tiles_per).index_select(0, s)               # tile number inside the species run
+    slot = j.unsqueeze(1) * nb + torch.arange(nb, dtype=torch.int64, device=device)
+    valid = used.unsqueeze(1) & (slot < counts.index_select(0, s).unsqueeze(1))
+    pos = torch.clamp(bounds.index_select(0, s).unsqueeze(1) + slot, max=max(n - 1, 0))
+    nodes = order.index_select(0, pos.flatten()).view(T, nb) if n else torch.zeros(T, nb, dtype=torch.int64,
+                                                                                      device=device)
+    tiles = torch.where(valid, nodes, torch.full_like(nodes, -1))
+    return tiles.contiguous(), s.to(torch.int32).contiguous()
 
 
 def species_node_tiles(species: torch.Tensor, num_elements: int):
@@ -88,11 +88,13 @@ def species_node_tiles(species: torch.Tensor, num_elements: int):
 
 
 class _Spec:
-    """Static part of one linear: species tiles (or None) and the output scale."""
+    """Static part of one linear: species tiles (or None), the output scale and the
+    degree of the first weight (the blocks are degrees degree0, degree0 + 1, ...)."""
 
-    def __init__(self, tiles, scale: float):
+    def __init__(self, tiles, scale: float, degree0: int = 0):
         self.tiles = tiles                    # None or (tiles, tile_species)
         self.scale = float(scale)
+        self.degree0 = int(degree0)
 
 
 def _launch(x, weights, spec: _Spec, out_width: int, cins: List[int], couts: List[int]):
@@ -106,9 +108,9 @@ def _launch(x, weights, spec: _Spec, out_width: int, cins: List[int], couts: Lis
     xo = yo = 0
     stream = stream_of(x)
     for l, w in enumerate(weights):
-        m = 2 * l + 1
+        m = 2 * (l + spec.degree0) + 1
         _native.call("ictc_channel_mix", ptr(x), int(x.shape[1]), xo, ptr(w), ptr(tiles), ptr(tspecies), num_tiles,
-                     ptr(y), int(out_width), yo, int(n), cins[l], couts[l], l, spec.scale, 0, stream)
+                     ptr(y), int(out_width), yo, int(n), cins[l], couts[l], l + spec.degree0, spec.scale, 0, stream)
         xo += cins[l] * m
         yo += couts[l] * m
     return y
@@ -123,7 +125,7 @@ class _ChannelMix(torch.autograd.Function):
         ctx.save_for_backward(x, *weights)
         couts = [w.shape[-2] for w in weights]
         cins = [w.shape[-1] for w in weights]
-        width = sum(c * (2 * l + 1) for l, c in enumerate(couts))
+        width = sum(c * (2 * (l + spec.degree0) + 1) for l, c in enumerate(couts))
         return _launch(x, [w.contiguous() for w in weights], spec, width, cins, couts)
 
     @staticmethod
@@ -140,7 +142,7 @@ class _ChannelMix(torch.autograd.Function):
         xo = yo = 0
         n = x.shape[0]
         for l, w in enumerate(weights):
-            m = 2 * l + 1
+            m = 2 * (l + spec.degree0) + 1
             cout, cin = w.shape[-2], w.shape[-1]
             if need[1 + l]:
                 gl = gy[:, yo:yo + cout * m].reshape(n, cout, m)
@@ -177,3 +179,59 @@ def channel_mix(x: torch.Tensor, weights: Sequence[torch.Tensor], scale: float =
     ws = [w if w.dim() == 3 else w.unsqueeze(0) for w in weights]
     out = _ChannelMix.apply(spec, x.contiguous(), *ws)
     return out
+
+
+# ---------------------------------------------------------------------------
+# Reference backend entry points (``ictc_o3/backends/ascend/linear.py:8,24``)
+# ---------------------------------------------------------------------------
+
+def _block_degree(features: torch.Tensor) -> int:
+    m = features.shape[-1]
+    if m % 2 == 0 or m > 7:
+        raise ValueError("The angular axis must have 2l+1 components with l <= 3")
+    return (m - 1) // 2
+
+
+def channel_linear(features: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None):
+    """features [..., I, M], weight [O, I], optional bias [O] (scalar blocks only) -> [..., O, M].
+
+    One degree block through the channel-mix kernel; first and higher derivatives
+    stay live (the weight gradient is a device reduction)."""
+    tensors = (features, weight) + (() if bias is None else (bias,))
+    if any(t.dtype != torch.float32 or t.device.type != "cuda" for t in tensors):
+        raise ValueError("the CUDA channel linear requires CUDA FP32 tensors")
+    if features.ndim < 2 or weight.ndim != 2 or features.shape[-2] != weight.shape[1]:
+        raise ValueError("Expected features [...,I,M] and weight [O,I]")
+    if bias is not None and (features.shape[-1] != 1 or bias.shape != (weight.shape[0],)):
+        raise ValueError("Bias is allowed only for scalar angular blocks with shape [O]")
+    degree = _block_degree(features)
+    lead, (cin, m) = features.shape[:-2], features.shape[-2:]
+    flat = features.reshape(-1, cin * m)
+    out = _ChannelMix.apply(_Spec(None, 1.0, degree), flat.contiguous(), weight.unsqueeze(0))
+    out = out.reshape(*lead, weight.shape[0], m)
+    return out if bias is None else out + bias.unsqueeze(-1)
+
+
+def species_channel_linear(features: torch.Tensor, weight: torch.Tensor, species: torch.Tensor,
+                           bias: Optional[torch.Tensor] = None):
+    """features [N, I, M], weight bank [S, O, I], species [N], optional bias [S, O] -> [N, O, M].
+
+    Every node uses its species' weights (species-homogeneous node tiles, no [N, O, I]
+    temporary and no host sort)."""
+    tensors = (features, weight) + (() if bias is None else (bias,))
+    if any(t.dtype != torch.float32 or t.device.type != "cuda" for t in tensors):
+        raise ValueError("the CUDA species channel linear requires CUDA FP32 tensors")
+    if (features.ndim != 3 or weight.ndim != 3 or features.shape[1] != weight.shape[2]
+            or species.shape != (features.shape[0],) or species.device != features.device
+            or species.dtype not in (torch.int32, torch.int64) or weight.shape[0] < 1):
+        raise ValueError("Expected features [N,I,M], weight [S,O,I] and integer species [N]")
+    from .species import validate_species
+    validate_species(species, weight.shape[0])
+    if bias is not None and (features.shape[-1] != 1 or bias.shape != weight.shape[:2]):
+        raise ValueError("Bias is allowed only for scalar angular blocks with shape [S,O]")
+    degree = _block_degree(features)
+    n, cin, m = features.shape
+    tiles = species_node_tiles(species, weight.shape[0])
+    out = _ChannelMix.apply(_Spec(tiles, 1.0, degree), features.reshape(n, cin * m).contiguous(), weight)
+    out = out.reshape(n, weight.shape[1], m)
+    return out if bias is None else out + bias.index_select(0, species.to(torch.int64)).unsqueeze(-1)

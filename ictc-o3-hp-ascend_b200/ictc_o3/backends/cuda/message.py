@@ -187,3 +187,40 @@ def graph_message(owner, features: Dict[int, torch.Tensor], harmonics: Dict[int,
     y = torch.cat([harmonics[l].reshape(edges, 2 * l + 1) for l in range(edge_lmax + 1)], 1)
     out = packed_graph_message(owner, "mul_ir", x, y, gates, src, dst, mask)
     return split_output(owner, out)
+
+
+def radial_graph_message(owner, features: Dict[int, torch.Tensor], harmonics: Dict[int, torch.Tensor], radial,
+                         edge_features: torch.Tensor, src, dst, mask=None, *, edge_chunk_size=None):
+    """Message whose gates come from the interaction's radial network
+    (``backends/ascend/capacity_message.py:109``; hook site ``pure_cartesian_ictd_fix.py:1787-1800``).
+
+    ``radial`` is the block's ``fc`` (``nn.Sequential`` of four bias-free Linear layers,
+    hidden width 64, with normalised SiLU modules between them: modules whose
+    ``_scale`` is 1.6791767923989418, as the reference's ``_Normalize2MomSiLU``).  Its gates are produced
+    by the fused tensor-core radial kernels, which keep the hidden activations on
+    chip, and fed to ``graph_message``.  Returns None (the caller keeps its own path)
+    when ``radial`` is not that network or its last layer does not produce P*C gates,
+    as the reference does for networks it does not stream."""
+    from . import radial as radial_kernels
+    if edge_chunk_size is not None and (not isinstance(edge_chunk_size, int) or isinstance(edge_chunk_size, bool)
+                                        or edge_chunk_size < 1):
+        raise ValueError("Edge chunk size must be positive")
+    if type(radial) is not torch.nn.Sequential or len(radial) == 0:
+        return None
+    linears = [m for m in radial if isinstance(m, torch.nn.Linear)]
+    acts = [m for m in radial if not isinstance(m, torch.nn.Linear)]
+    if (len(linears) != 4 or len(acts) != 3 or any(m.bias is not None for m in linears)
+            or not isinstance(radial[-1], torch.nn.Linear)
+            or any(getattr(m, "_scale", None) != radial_kernels.SILU_SCALE for m in acts)):
+        return None
+    sample = next(iter(features.values()))
+    if linears[-1].out_features != owner.num_paths * sample.shape[1]:
+        return None
+    shape = (linears[0].in_features, linears[0].out_features, linears[-1].out_features)
+    if not radial_kernels.supported(*shape):
+        return None
+    plan = radial.__dict__.get("_ictc_radial_plan")
+    if plan is None:
+        plan = radial.__dict__["_ictc_radial_plan"] = radial_kernels.RadialPlan()
+    gates = radial_kernels.radial_gates(linears, edge_features, plan)
+    return graph_message(owner, features, harmonics, gates, src, dst, mask, edge_chunk_size=edge_chunk_size)

@@ -36,13 +36,24 @@ def mlp_reference(feats, weights):
     return h @ w4.t()
 
 
+GATE_TILE = 64
+
+
+def padded_gates(gates: int) -> int:
+    """The kernels write gate rows in 64-column chunks; other widths run on W4 padded with
+    zero rows to the next multiple of 64 (the extra columns are dropped)."""
+    return -(-int(gates) // GATE_TILE) * GATE_TILE
+
+
 def supported(features: int, hidden: int, gates: int) -> bool:
-    return int(_native.library().ictc_radial_image_bytes(features, hidden, gates)) > 0
+    return gates > 0 and int(_native.library().ictc_radial_image_bytes(features, hidden, padded_gates(gates))) > 0
 
 
 def pack_image(weights) -> torch.Tensor:
     """Host-packed TF32 hi/lo image of the four weights, uploaded to the weights' device."""
     w1, w2, w3, w4 = (w.detach().to("cpu", torch.float32).contiguous() for w in weights)
+    if w4.shape[0] % GATE_TILE:
+        w4 = torch.cat([w4, w4.new_zeros(padded_gates(w4.shape[0]) - w4.shape[0], w4.shape[1])])
     features, gates = w1.shape[1], w4.shape[0]
     lib = _native.library()
     size = int(lib.ictc_radial_image_bytes(features, HIDDEN, gates))
@@ -95,7 +106,9 @@ class _Radial(torch.autograd.Function):
     @staticmethod
     def forward(ctx, feats, image, status, w1, w2, w3, w4):
         ctx.save_for_backward(feats, image, status, w1, w2, w3, w4)
-        return _forward(image, status, feats, w4.shape[0])
+        gates = w4.shape[0]
+        out = _forward(image, status, feats, padded_gates(gates))
+        return out if out.shape[1] == gates else out[:, :gates].contiguous()
 
     @staticmethod
     def backward(ctx, grad):
@@ -112,7 +125,10 @@ class _Radial(torch.autograd.Function):
                                                  allow_unused=True))
             result = [grads.pop(0) if n else None for n in need]
             return result[0], None, None, result[1], result[2], result[3], result[4]
-        return _backward(image, status, feats, grad.contiguous()), None, None, None, None, None, None
+        grad = grad.contiguous()
+        if grad.shape[1] % GATE_TILE:
+            grad = torch.nn.functional.pad(grad, (0, padded_gates(grad.shape[1]) - grad.shape[1]))
+        return _backward(image, status, feats, grad), None, None, None, None, None, None
 
 
 def radial_gates(linears, feats: torch.Tensor, plan: RadialPlan) -> torch.Tensor:

@@ -135,6 +135,61 @@ def from_reference_state_dict(model, state: Dict[str, torch.Tensor], strict: boo
     return accepted
 
 
+# Architecture metadata a reference checkpoint must carry (the keys the reference's
+# multi-device engine requires, ``mace_ictc/interfaces/ascend_lammps.py:50-53``).
+REQUIRED_METADATA = ("channel_in", "lmax", "num_interaction", "avg_num_neighbors", "radial_sqrt_num_basis",
+                     "polynomial_cutoff_p", "ictd_fix_product_backend")
+
+
+def model_metadata(model) -> Dict[str, object]:
+    """The reference metadata values that describe ``model``."""
+    return {"channel_in": model.channels, "lmax": model.lmax, "num_interaction": len(model.interactions),
+            "avg_num_neighbors": model.avg_num_neighbors, "radial_sqrt_num_basis": model.radial_sqrt_num_basis,
+            "polynomial_cutoff_p": model.p, "ictd_fix_product_backend": "ictd-pure-u",
+            "ictd_fix_first_layer_self_connection": model.first_layer_self_connection,
+            "max_radius": model.r_max, "tensor_product_mode": "pure-cartesian-ictd-fix", "dtype": "float32"}
+
+
+def check_reference_metadata(model, metadata: Dict[str, object]):
+    """Raise unless a reference checkpoint's architecture metadata describes ``model``.
+
+    The state dict alone does not show every choice that changes the energy (the
+    radial embedding's sqrt(num_basis) factor has no parameter), so a checkpoint
+    whose metadata is missing or differs is refused rather than loaded into a model
+    that would give different energies."""
+    missing = [k for k in REQUIRED_METADATA if k not in metadata]
+    if missing:
+        raise ValueError(f"Missing model metadata: {missing}; re-save with the training configuration")
+    want = model_metadata(model)
+    bad = []
+    for key, value in metadata.items():
+        if key not in want:
+            continue
+        mine = want[key]
+        if isinstance(mine, float) or isinstance(value, float):
+            same = abs(float(value) - float(mine)) <= 1e-9 * max(1.0, abs(float(mine)))
+        elif isinstance(mine, bool):
+            same = bool(value) == mine
+        else:
+            same = str(value).replace("torch.", "") == str(mine)
+        if not same:
+            bad.append(f"{key}: checkpoint {value!r}, model {mine!r}")
+    if bad:
+        raise ValueError("checkpoint does not describe this model: " + "; ".join(bad))
+
+
+def load_reference_checkpoint(model, checkpoint: Dict[str, object], strict: bool = True) -> List[str]:
+    """Load a reference training checkpoint (``Trainer.save_checkpoint``,
+    ``mace_ictc/training/train_loop.py:2053-2077``): metadata check, then the weights
+    of ``e3trans_state_dict``.  Returns the keys accepted as identities."""
+    metadata = dict(checkpoint.get("model_hyperparameters", {}) or {})
+    for key in ("dtype", "max_radius", "tensor_product_mode"):
+        if key in checkpoint:
+            metadata[key] = checkpoint[key]
+    check_reference_metadata(model, metadata)
+    return from_reference_state_dict(model, checkpoint["e3trans_state_dict"], strict=strict)
+
+
 def to_reference_state_dict(model) -> Dict[str, torch.Tensor]:
     """The inverse mapping: a state dict with the reference's names and layouts."""
     out: Dict[str, torch.Tensor] = {"node_embedding.weight": model.node_embedding.weight.detach().clone()}

@@ -19,7 +19,9 @@ Structure of the reference model (``mace_ictc/models/pure_cartesian_ictd_fix.py`
 
 The three hot operators (edge harmonics, TP graph message, symmetric
 contraction) are taken from an ``ops`` object; the default is the CUDA backend.
-Dense channel mixing runs as cuBLAS FP32 GEMMs with TF32 disabled.
+On CUDA tensors the per-degree channel linears run as the backend's channel-mix
+kernel and the radial MLP as its fused tensor-core kernels; on CPU tensors (tests
+with the oracle ops) the same modules use plain torch matrix products.
 """
 from __future__ import annotations
 
@@ -43,10 +45,10 @@ class CudaOps:
         from ictc_o3.backends.cuda.geometry import direction_harmonics
         return direction_harmonics(n, lmax)
 
-    def edge_geometry(self, vec, r_max, num_basis, p):
+    def edge_geometry(self, vec, r_max, num_basis, p, basis_norm=True):
         """(unit vectors, radial embedding, cutoff mask): one fused kernel each way."""
         from ictc_o3.backends.cuda.geometry import edge_geometry
-        return edge_geometry(vec, r_max, num_basis, p)
+        return edge_geometry(vec, r_max, num_basis, p, basis_norm)
 
     def message(self, tp, features, harmonics, gates, src, dst, mask, dst_nodes):
         from ictc_o3.backends.cuda.message import packed_graph_message
@@ -56,16 +58,17 @@ class CudaOps:
         return module(features, node_type_idx=species)
 
     def radial(self, fc, feats):
-        """Gates of the radial MLP: fused tensor-core kernels when the shape is supported."""
+        """Gates of the radial MLP on the fused tensor-core kernels; a shape the kernels do
+        not support raises (there is no library fallback)."""
         from ictc_o3.backends.cuda import radial
         linears = [m for m in fc if isinstance(m, nn.Linear)]
         shape = (linears[0].in_features, linears[0].out_features, linears[-1].out_features)
         plan = fc.__dict__.get("_ictc_radial_plan")
         if plan is None:
-            plan = radial.RadialPlan() if radial.supported(*shape) else False
-            fc.__dict__["_ictc_radial_plan"] = plan
-        if plan is False:
-            return fc(feats)
+            if not radial.supported(*shape):
+                raise ValueError(f"radial MLP shape (features, hidden, gates) = {shape} is not supported by the "
+                                 "fused radial kernels")
+            plan = fc.__dict__["_ictc_radial_plan"] = radial.RadialPlan()
         return radial.radial_gates(linears, feats, plan)
 
 
@@ -91,6 +94,8 @@ def radial_embedding(r, r_max, num_basis=8, p=5, sqrt_num_basis_norm=True):
 
 
 class NormalizedSiLU(nn.Module):
+    _scale = SILU_SCALE
+
     def forward(self, x):
         return F.silu(x) * SILU_SCALE
 
@@ -111,7 +116,7 @@ def _blocks(x, widths, lmax):
 
 def _merge(blocks):
     n = blocks[0].shape[0]
-    return torch.cat([b.reshape(n, -1) for b in blocks], -1)
+    return torch.cat([b.reshape(n, b.shape[1] * b.shape[2]) for b in blocks], -1)
 
 
 class ChannelLinearSO3(nn.Module):
@@ -217,13 +222,21 @@ class InteractionBlock(nn.Module):
                                                                                   init="identity")
 
     def forward(self, ops, node_feats, edge_harmonics, edge_feats, src, dst, mask, groups, owned=None,
-                species=None):
+                species=None, exchange=None):
         """Messages into the first ``owned`` nodes (all nodes by default); ``groups`` and
-        ``species`` (the owned nodes' species) select the element-conditioned weights."""
+        ``species`` (the owned nodes' species) select the element-conditioned weights.
+
+        With ``exchange`` (spatial decomposition), ``node_feats`` holds the owned rows
+        only: ``linear_up`` runs on them (it acts row by row, so it commutes with the
+        halo copy and no ghost row is transformed), their ghost copies travel to the
+        neighbours while the radial MLP runs, and the message reads the local rows."""
         owned = node_feats.shape[0] if owned is None else owned
         x_up = self.linear_up(node_feats)
+        pending = exchange(x_up) if exchange is not None else None
         radial = getattr(ops, "radial", None)
         gates = radial(self.fc, edge_feats) if radial is not None else self.fc(edge_feats)
+        if pending is not None:
+            x_up = pending.finish()
         msg = ops.message(self.tp, x_up, edge_harmonics, gates, src, dst, mask, owned)
         message = self.message_linear(msg, scale=1.0 / max(self.avg_num_neighbors, 1e-8))
         if self.self_connection is None:
@@ -254,21 +267,44 @@ class ProductBlock(nn.Module):
 class MACEICTC(nn.Module):
     """MACE-ICTC energy model; ``energy(...)`` and ``energy_and_forces(...)``."""
 
-    def __init__(self, *, num_elements=3, channels=64, lmax=2, num_interactions=2, correlation=3, r_max=5.0,
-                 num_basis=8, polynomial_cutoff_p=5, avg_num_neighbors=1.0, readout_hidden=16, ops=None):
+    def __init__(self, *, num_elements=None, channels=64, lmax=2, num_interactions=2, correlation=3, r_max=5.0,
+                 num_basis=8, polynomial_cutoff_p=5, avg_num_neighbors=1.0, readout_hidden=16, ops=None,
+                 atomic_numbers=(1, 6, 8), first_layer_self_connection=True, radial_sqrt_num_basis=False):
+        """Defaults follow the reference constructor for new models: atomic numbers
+        H, C, O (``mace_ictc/hp/runtime.py:7``), an element-conditioned scalar
+        self-connection in the first layer (``mace_ictc/models/factory.py:17``,
+        ``pure_cartesian_ictd_fix.py:2393-2395``) and the radial embedding without
+        the sqrt(num_basis) factor (``radial_sqrt_num_basis=False``, :2191, :2325).
+        ``num_elements`` (if given) must equal ``len(atomic_numbers)``."""
         super().__init__()
+        atomic_numbers = tuple(sorted({int(z) for z in atomic_numbers}))
+        if not atomic_numbers or atomic_numbers[0] < 0:
+            raise ValueError("atomic_numbers must be non-negative and not empty")
+        if num_elements is not None and num_elements != len(atomic_numbers):
+            atomic_numbers = tuple(range(1, num_elements + 1))   # anonymous elements 1..S
+        self.atomic_numbers = atomic_numbers
+        num_elements = len(atomic_numbers)
+        table = torch.full((max(atomic_numbers) + 1,), -1, dtype=torch.long)
+        table[list(atomic_numbers)] = torch.arange(num_elements)
+        self.register_buffer("atomic_number_to_index", table, persistent=False)
         self.num_elements, self.channels, self.lmax = num_elements, channels, lmax
         self.r_max, self.num_basis, self.p = float(r_max), num_basis, polynomial_cutoff_p
+        self.first_layer_self_connection = bool(first_layer_self_connection)
+        self.radial_sqrt_num_basis = bool(radial_sqrt_num_basis)
+        self.avg_num_neighbors = float(avg_num_neighbors)
+        self.correlation = int(correlation)
+        self.preserve_edge_order = False
         self.ops = CudaOps() if ops is None else ops
         self.node_embedding = nn.Linear(num_elements, channels, bias=False)
         self.interactions = nn.ModuleList()
         self.products = nn.ModuleList()
         for layer in range(num_interactions):
             target = lmax if layer < num_interactions - 1 else 0
+            first_sc = self.first_layer_self_connection and layer == 0
             self.interactions.append(InteractionBlock(
                 channels=channels, lmax=lmax, input_lmax=0 if layer == 0 else lmax, num_elements=num_elements,
-                num_basis=num_basis, avg_num_neighbors=avg_num_neighbors, use_self_connection=layer > 0,
-                sc_lmax=target))
+                num_basis=num_basis, avg_num_neighbors=avg_num_neighbors, use_self_connection=layer > 0 or first_sc,
+                sc_lmax=0 if first_sc else target))
             self.products.append(ProductBlock(channels=channels, lmax=lmax, target_lmax=target,
                                               correlation=correlation, num_elements=num_elements))
         self.layer_readouts = nn.ModuleList([nn.Linear(channels, 1, bias=False)
@@ -285,11 +321,11 @@ class MACEICTC(nn.Module):
         """Harmonics, radial embedding and cutoff mask of edge vectors r_e = pos[dst] - pos[src] + shift."""
         geometry = getattr(self.ops, "edge_geometry", None)
         if geometry is not None:
-            n, feats, mask = geometry(vec, self.r_max, self.num_basis, self.p)
+            n, feats, mask = geometry(vec, self.r_max, self.num_basis, self.p, self.radial_sqrt_num_basis)
         else:
             length = vec.norm(dim=1)
             n = vec / length.clamp_min(1e-8).unsqueeze(-1)
-            feats = radial_embedding(length, self.r_max, self.num_basis, self.p)
+            feats = radial_embedding(length, self.r_max, self.num_basis, self.p, self.radial_sqrt_num_basis)
             mask = (length <= self.r_max).to(vec.dtype).detach()
         harmonics = self.ops.harmonics(n, self.lmax)
         return harmonics, feats, mask
@@ -302,36 +338,46 @@ class MACEICTC(nn.Module):
         return self.node_energies_from_vectors(self.edge_vectors(pos, src, dst, shift_vectors), species, src, dst,
                                                layers=layers)
 
-    def node_energies_from_vectors(self, vec, species, src, dst, layers=None, owned=None, exchange=None):
+    def node_energies_from_vectors(self, vec, species, src, dst, layers=None, owned=None, exchange=None,
+                                   phases=None, owned_species=None):
         """Energies of the first ``owned`` nodes from edge vectors.
 
         Spatial decomposition (``mace_ictc/interfaces/ascend_lammps.py:286-333``,
         compact owned outputs): rows ``[0, owned)`` are this rank's atoms and the rest
         are ghost copies; every edge's receiver ``dst`` is an owned row.  Messages,
-        products and readouts run on owned rows only, and before each later layer
-        ``exchange`` maps the owned features [owned, W] to all local rows (owned rows
-        followed by the ghosts' features from their owners).
+        products and readouts run on owned rows only, and in each later layer
+        ``exchange`` starts the copy of the owned rows [owned, W] to the neighbours
+        (its ``finish()`` gives all local rows: owned rows followed by the ghosts'
+        rows from their owners).  ``phases`` (a ``StepPhases``) receives marks.
+        ``owned_species`` may pass the owned rows' species as a tensor that lives
+        across steps (its species tiles are then built once, not every step).
         """
         n_local = species.shape[0]
         owned = n_local if owned is None else int(owned)
         if owned != n_local and exchange is None:
             raise ValueError("ghost rows need an exchange to refresh their features")
         own_species = species if owned == n_local else species[:owned]
+        if owned_species is not None:
+            if owned_species.shape != (owned,):
+                raise ValueError("owned_species must hold one species per owned row")
+            own_species = owned_species
         # The CUDA linears take species directly; node index groups serve the torch path.
         groups = None if species.is_cuda else species_groups(own_species, self.num_elements)
+        mark = (lambda name: phases.mark(name, vec.device)) if phases is not None else (lambda name: None)
         harmonics, feats, mask = self.edge_features(vec)
+        mark("edge_geometry")
         h = self.node_embedding.weight.t().index_select(0, species)
         energy = None
         count = len(self.interactions) if layers is None else layers
         for layer in range(count):
-            if layer and exchange is not None:
-                h = exchange(h)
             message, sc = self.interactions[layer](self.ops, h, harmonics, feats, src, dst, mask, groups, owned,
-                                                   own_species)
+                                                   own_species, exchange=exchange if layer else None)
+            mark(f"layer{layer}.interaction")
             h = self.products[layer](self.ops, message, sc, own_species)
             readout = (self.layer_readouts[layer](h[:, :self.channels]) if layer < len(self.interactions) - 1
                        else self.last_readout(h[:, :self.channels]))
             energy = readout if energy is None else energy + readout
+            mark(f"layer{layer}.product")
         return energy.squeeze(-1)
 
     def energy(self, pos, species, src, dst, shift_vectors=None, batch=None, num_graphs=1):

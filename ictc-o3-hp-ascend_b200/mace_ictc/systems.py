@@ -1,4 +1,4 @@
-"""Synthetic atomic systems of the benchmark configurations.
+"""Synthetic atomic systems of the benchmark configurations (benchmark configs 3-5: 0.1 atoms per cubic angstrom).
 
 H/C/O atoms with uniformly random species, placed uniformly at random in a
 periodic cube at a given number density with a minimum pair distance (0.9 A):

@@ -18,7 +18,7 @@ class OracleOps:
     def message(self, tp, features, harmonics, gates, src, dst, mask, dst_nodes):
         li = max(p[0] for p in tp.paths)
         out = tp_oracle.graph_message(tp, tp_oracle.split_mul_ir(features, tp.channels, li),
-                                      tp_oracle.split_harm(harmonics, tp.lmax), gates.view(gates.shape[0], -1, tp.channels),
+                                      tp_oracle.split_harm(harmonics, tp.lmax), gates.view(gates.shape[0], tp.num_paths, tp.channels),
                                       src, dst, mask, nodes=dst_nodes, dtype=self.dtype)
         return tp_oracle.pack_out(tp, out)
 

@@ -26,7 +26,7 @@ def contraction(u_tensors, weights_max, weights, x, idx, output_l):
         out = torch.einsum("bc...i,bci->bc...", out, x)
         out = out + selected_coefficient(u_tensors[order], weight, idx, output_l)
     out = torch.einsum("bc...i,bci->bc...", out, x)
-    return out.reshape(out.shape[0], -1)
+    return out.reshape(out.shape[0], out[0].numel() if out.shape[0] else out.shape[1] * (2 * output_l + 1))
 
 
 def flat_to_mace(flat, channels, lmax):

@@ -127,7 +127,7 @@ def blocks_to_packed_output(owner, blocks, layout):
         value = blocks[l].reshape(rows, count, owner.channels, 2 * l + 1)
         if layout == "ir_mul":
             value = value.transpose(2, 3)
-        parts.append(value.reshape(rows, -1))
+        parts.append(value.reshape(rows, count * owner.channels * (2 * l + 1)))
     return torch.cat(parts, -1)
 
 

@@ -69,3 +69,36 @@ def test_identity_options_accepted_others_rejected():
     ref["interactions.0.attn_q_proj.weight"] = torch.zeros(8, 8, dtype=torch.float64)
     with pytest.raises(NotImplementedError):
         from_reference_state_dict(model, ref)
+
+
+def test_checkpoint_metadata_is_checked():
+    """A reference checkpoint whose metadata differs from the model (e.g. the radial
+    embedding's sqrt(num_basis) factor, which no parameter shows) is refused."""
+    from mace_ictc.checkpoint import load_reference_checkpoint, model_metadata, to_reference_state_dict
+    model = _model(5)
+    meta = {k: v for k, v in model_metadata(model).items()}
+    ckpt = {"e3trans_state_dict": to_reference_state_dict(model), "model_hyperparameters": meta,
+            "dtype": "float32", "tensor_product_mode": "pure-cartesian-ictd-fix"}
+    load_reference_checkpoint(model, ckpt)
+    for key, value in (("radial_sqrt_num_basis", True), ("ictd_fix_product_backend", "ictd-bridge-u"),
+                       ("ictd_fix_first_layer_self_connection", False), ("avg_num_neighbors", 7.5),
+                       ("lmax", 3)):
+        bad = dict(ckpt, model_hyperparameters=dict(meta, **{key: value}))
+        with pytest.raises(ValueError):
+            load_reference_checkpoint(model, bad)
+    missing = dict(ckpt, model_hyperparameters={k: v for k, v in meta.items() if k != "radial_sqrt_num_basis"})
+    with pytest.raises(ValueError):
+        load_reference_checkpoint(model, missing)
+
+
+def test_model_defaults_follow_the_reference_constructor():
+    """Reference defaults for new models: no sqrt(num_basis) radial factor, first-layer
+    scalar self-connection (no message selector), atomic numbers H, C, O."""
+    from mace_ictc.models import MACEICTC
+    model = MACEICTC(channels=8, lmax=2)
+    assert model.radial_sqrt_num_basis is False
+    assert model.first_layer_self_connection is True
+    first = model.interactions[0]
+    assert first.self_connection is not None and first.message_selector is None and first.sc_lmax == 0
+    assert model.atomic_numbers == (1, 6, 8)
+    assert model.atomic_number_to_index.tolist()[:9] == [-1, 0, -1, -1, -1, -1, 1, -1, 2]

@@ -1,4 +1,11 @@
-"""Spatial decomposition on the GPU: slab edge lists, and NCCL halo exchange on 2 GPUs."""
+"""Spatial decomposition on GPUs: NCCL ranks (2, 4, 8 B200) against one GPU.
+
+Every rank runs ``md_step`` (migration, ghost positions over NCCL, owned-receiver
+neighbour list, model with the feature halo and its adjoint, ghost-force return,
+energy/virial all-reduce).  The parent process compares energy, forces and
+virial with the single-GPU evaluation of the same configuration, and checks that
+the ranks' edges, mapped to global atoms, are exactly the global neighbour list.
+"""
 import os
 import socket
 from datetime import timedelta
@@ -15,82 +22,65 @@ pytestmark = pytest.mark.gpu
 CUTOFF = 5.0
 
 
-def _edge_keys(src, dst, vec, n):
-    key = dst * n + src
-    order = torch.argsort(key)
-    return key[order], vec[order]
-
-
-@pytest.mark.parametrize("world", [2, 3, 4])
-def test_slab_edges_cover_global_neighbour_list(world, cuda_device):
-    """Every rank's owned-receiver edges, mapped to global atoms, together are exactly the
-    global neighbour list, with the same edge vectors."""
-    from ictc_o3.backends.cuda.neighbors import neighbor_list
-    from mace_ictc.parallel import local_positions, slab_edges, slab_layout
-    from mace_ictc.systems import random_system
-    n = 6000
-    pos, _, side = random_system(n, seed=5, device=cuda_device)
-    src, dst, shift, _ = neighbor_list(pos, (side,) * 3, CUTOFF)
-    ref_key, ref_vec = _edge_keys(src, dst, pos[dst] - pos[src] + shift, n)
-    keys, vecs = [], []
-    for rank in range(world):
-        layout = slab_layout(pos, side, rank, world, CUTOFF)
-        p = local_positions(layout, pos, side)
-        s, d, sh = slab_edges(layout, p, side, CUTOFF, CUTOFF)
-        assert int(d.max()) < layout.owned
-        assert bool((d[1:] >= d[:-1]).all()), "edges grouped by receiver"
-        g = layout.local_global
-        keys.append(g[d] * n + g[s])
-        vecs.append(p[d] - p[s] + sh)
-    key = torch.cat(keys)
-    order = torch.argsort(key)
-    assert torch.equal(key[order], ref_key)
-    torch.testing.assert_close(torch.cat(vecs)[order], ref_vec, rtol=0, atol=2e-4)
-
-
 def _model(channels=32):
     from mace_ictc.models import MACEICTC
     torch.manual_seed(5)
     return MACEICTC(channels=channels, lmax=2, r_max=CUTOFF, avg_num_neighbors=40.0)
 
 
-def test_single_rank_decomposition_matches_model(cuda_device):
-    """world = 1: distributed_energy_forces equals energy_and_forces of the same model."""
-    from ictc_o3.backends.cuda.neighbors import neighbor_list
-    from mace_ictc.parallel import distributed_energy_forces, local_positions, slab_edges, slab_layout
+def _system(n_atoms, seed, device, x_fraction=1.0):
+    """Random system; with ``x_fraction`` < 1 only atoms with x below that fraction of the
+    box are kept (the rest of x is vacuum, so some slabs own nothing)."""
     from mace_ictc.systems import random_system
-    pos, species, side = random_system(3000, seed=6, device=cuda_device)
+    pos, species, side = random_system(n_atoms, seed=seed, device=device)
+    if x_fraction < 1.0:
+        keep = pos[:, 0] < x_fraction * side
+        pos, species = pos[keep].contiguous(), species[keep].contiguous()
+    return pos, species, side
+
+
+def _one_gpu(pos, species, side, model):
+    """Single-process reference: energy, forces in atom order, virial, sorted edge keys/vectors."""
+    from mace_ictc.parallel import md_step, partition
+    domain = partition(pos, species, side, 0, 1, CUTOFF)
+    domain, e, f, w = md_step(model, domain, CUTOFF)
+    forces = torch.empty_like(f)
+    forces[domain.ids] = f
+    return e, forces, w
+
+
+def test_single_rank_decomposition_matches_model(cuda_device):
+    """world = 1: md_step equals energy_and_forces of the same model."""
+    from ictc_o3.backends.cuda.neighbors import neighbor_list
+    pos, species, side = _system(3000, 6, cuda_device)
     model = _model().to(cuda_device)
     src, dst, shift, _ = neighbor_list(pos, (side,) * 3, CUTOFF)
     e_ref, f_ref = model.energy_and_forces(pos, species, src, dst, shift)
-    layout = slab_layout(pos, side, 0, 1, CUTOFF)
-    p = local_positions(layout, pos, side)
-    s, d, sh = slab_edges(layout, p, side, CUTOFF, CUTOFF)
-    e, f, w = distributed_energy_forces(model, layout, p, species[layout.local_global], s, d, sh)
+    e, f, w = _one_gpu(pos, species, side, model)
     assert_close(e, e_ref, 1e-5, what="energy")
-    f_global = torch.empty_like(f)
-    f_global[layout.local_global] = f
-    assert_close(f_global, f_ref, 1e-4, what="forces")
+    assert_close(f, f_ref, 1e-4, what="forces")
     assert w.shape == (6,)
 
 
-def _nccl_worker(rank, world, port, out_dir, n_atoms):
+def _nccl_worker(rank, world, port, out_dir, n_atoms, x_fraction):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     device = torch.device("cuda", rank)
     torch.cuda.set_device(device)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=device)
     try:
-        from mace_ictc.parallel import distributed_energy_forces, local_positions, slab_edges, slab_layout
-        from mace_ictc.systems import random_system
-        pos, species, side = random_system(n_atoms, seed=8, device=device)
+        from mace_ictc.parallel import distributed_energy_forces, exchange_atoms, partition, slab_edges
+        pos, species, side = _system(n_atoms, 8, device, x_fraction)
         model = _model().to(device)
-        layout = slab_layout(pos, side, rank, world, CUTOFF)
-        p = local_positions(layout, pos, side)
-        s, d, sh = slab_edges(layout, p, side, CUTOFF, CUTOFF)
-        e, f, w = distributed_energy_forces(model, layout, p, species[layout.local_global], s, d, sh)
-        torch.save({"owned": layout.local_global[:layout.owned].cpu(), "energy": e.cpu(), "forces": f.cpu(),
-                    "virial": w.cpu()}, os.path.join(out_dir, f"rank{rank}.pt"))
+        domain, layout, p, s = exchange_atoms(partition(pos, species, side, rank, world, CUTOFF))
+        src, dst, shift = slab_edges(layout, p, CUTOFF)
+        e, f, w = distributed_energy_forces(model, layout, p, s, src, dst, shift, owned_species=domain.species)
+        ids = layout.local_ids
+        torch.save({"owned": domain.ids.cpu(), "energy": e.cpu(), "forces": f.cpu(), "virial": w.cpu(),
+                    "edge_keys": (ids[dst] * pos.shape[0] + ids[src]).cpu(), "edge_vecs": (p[dst] - p[src] + shift).cpu(),
+                    "receivers_owned": bool(dst.numel() == 0 or int(dst.max()) < layout.owned)},
+                   os.path.join(out_dir, f"rank{rank}.pt"))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -102,27 +92,43 @@ def _free_port():
         return sock.getsockname()[1]
 
 
-def test_two_gpu_halo_exchange_matches_one_gpu(cuda_device, tmp_path):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    from mace_ictc.parallel import distributed_energy_forces, local_positions, slab_edges, slab_layout
-    from mace_ictc.systems import random_system
-    n_atoms, world = 8000, 2
-    pos, species, side = random_system(n_atoms, seed=8, device=cuda_device)
+@pytest.mark.parametrize("world,x_fraction", [(2, 1.0), (4, 1.0), (8, 1.0), (4, 0.45)])
+def test_nccl_ranks_match_one_gpu(world, x_fraction, cuda_device, tmp_path):
+    """world ranks on world GPUs equal one GPU: energy 1e-5, forces and virial 1e-4, and
+    the union of the ranks' edges is the global neighbour list (x_fraction < 1: vacuum,
+    some ranks own no atoms)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from ictc_o3.backends.cuda.neighbors import neighbor_list
+    n_atoms = 4000 * world
+    pos, species, side = _system(n_atoms, 8, cuda_device, x_fraction)
     model = _model().to(cuda_device)
-    layout = slab_layout(pos, side, 0, 1, CUTOFF)
-    p = local_positions(layout, pos, side)
-    s, d, sh = slab_edges(layout, p, side, CUTOFF, CUTOFF)
-    e_ref, f_ref, w_ref = distributed_energy_forces(model, layout, p, species[layout.local_global], s, d, sh)
-    mp.start_processes(_nccl_worker, args=(world, _free_port(), str(tmp_path), n_atoms), nprocs=world, join=True,
-                       start_method="spawn")
-    forces = torch.full((n_atoms, 3), float("nan"))
-    f_ref_global = torch.empty(n_atoms, 3)
-    f_ref_global[layout.local_global.cpu()] = f_ref.cpu()
+    e_ref, f_ref, w_ref = _one_gpu(pos, species, side, model)
+    src, dst, shift, _ = neighbor_list(pos, (side,) * 3, CUTOFF)
+    n = pos.shape[0]
+    ref_key = dst * n + src
+    order = torch.argsort(ref_key)
+    ref_key, ref_vec = ref_key[order].cpu(), (pos[dst] - pos[src] + shift)[order].cpu()
+    mp.start_processes(_nccl_worker, args=(world, _free_port(), str(tmp_path), n_atoms, x_fraction), nprocs=world,
+                       join=True, start_method="spawn")
+    forces = torch.full((n, 3), float("nan"))
+    seen = torch.zeros(n, dtype=torch.long)
+    keys, vecs, empty = [], [], 0
     for rank in range(world):
         out = torch.load(tmp_path / f"rank{rank}.pt")
         forces[out["owned"]] = out["forces"]
+        seen[out["owned"]] += 1
+        empty += int(out["owned"].numel() == 0)
+        assert out["receivers_owned"]
+        keys.append(out["edge_keys"])
+        vecs.append(out["edge_vecs"])
         assert_close(out["energy"], e_ref.cpu(), 1e-5, what="energy")
         assert_close(out["virial"], w_ref.cpu(), 1e-4, what="virial")
-    assert not bool(torch.isnan(forces).any())
-    assert_close(forces, f_ref_global, 1e-4, what="forces")
+    assert bool((seen == 1).all()), "every atom owned by exactly one rank"
+    if x_fraction < 1.0:
+        assert empty >= 1, "the vacuum case has a rank without atoms"
+    assert_close(forces, f_ref.cpu(), 1e-4, what="forces")
+    key = torch.cat(keys)
+    order = torch.argsort(key)
+    assert torch.equal(key[order], ref_key)
+    torch.testing.assert_close(torch.cat(vecs)[order], ref_vec, rtol=0, atol=2e-4)

@@ -22,7 +22,8 @@ def _reference(feats, layers):
 
 
 @pytest.mark.parametrize("features,gates,edges", [(8, 704, 1000), (8, 192, 4096), (6, 512, 333),
-                                                  (8, 2944, 257), (8, 128, 128), (3, 320, 77)])
+                                                  (8, 2944, 257), (8, 128, 128), (3, 320, 77),
+                                                  (8, 96, 500), (8, 24, 129)])
 def test_radial_forward_and_embedding_gradient(features, gates, edges, cuda_device):
     from ictc_o3.backends.cuda import radial
     layers = [m.to(cuda_device) for m in _net(features, gates, edges)]

@@ -1,6 +1,6 @@
 """GPU parity of the CUDA tensor product against the reference (golden) and the oracle.
 
-Tolerances: relative L2 1e-5 on TP outputs, 1e-4 on
+Tolerances (the project's FP32 parity bar): relative L2 1e-5 on TP outputs, 1e-4 on
 gradients and second derivatives, plus the reference's componentwise bound
 (rtol 1e-4, atol 2e-5 scaled by the RMS; docs/USAGE.md:889-891); see _util.assert_close.
 """
