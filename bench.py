@@ -297,20 +297,77 @@ def mace_block(device, steps, warmup, atoms=16384, cpu_seconds=0.0):
     return result
 
 
-def mace_block_cpu(seconds, atoms=1024):
-    """The same block on the oracle ops (torch CPU FP32, all host threads), smaller system."""
-    from mace_ictc.models import InteractionBlock, ProductBlock, radial_embedding, species_groups
-    from oracle.model_ops import OracleOps
-    torch.set_num_threads(os.cpu_count() or 1)
-    gen = torch.Generator().manual_seed(3)
+def _cpu_system(atoms, seed, cutoff=5.0):
+    """Uniform random periodic system at 0.1 / A^3 with a brute-force minimum-image
+    neighbour list (host CPU; needs a box side above twice the cutoff)."""
+    gen = torch.Generator().manual_seed(seed)
     side = (atoms / 0.1) ** (1 / 3)
     pos = torch.rand(atoms, 3, generator=gen) * side
     species = torch.randint(0, 3, (atoms,), generator=gen)
     d = pos[None] - pos[:, None]
     s = -side * torch.round(d / side)
     dist = (d + s).norm(dim=-1)
-    i, j = torch.nonzero((dist < 5.0) & (dist > 0), as_tuple=True)
-    src, dst, shift = j, i, s[i, j]
+    i, j = torch.nonzero((dist < cutoff) & (dist > 0), as_tuple=True)
+    return pos, species, side, j, i, s[i, j]
+
+
+def mace_md_cpu(seconds, atoms=512):
+    """configs[4] step (E, F, virial of the C64/lmax2 model) on the oracle ops, torch CPU
+    FP32 with all host threads, on a small system: the port's CPU speed."""
+    from mace_ictc.models import MACEICTC
+    from mace_ictc.parallel import distributed_energy_forces, halo_layout, partition
+    from oracle.model_ops import OracleOps
+    torch.set_num_threads(os.cpu_count() or 1)
+    pos, species, side, src, dst, shift = _cpu_system(atoms, 9)
+    torch.manual_seed(0)
+    model = MACEICTC(channels=64, lmax=2, num_interactions=2, correlation=3, r_max=5.0, avg_num_neighbors=52.0,
+                     ops=OracleOps(torch.float32))
+    layout, p, sp = halo_layout(partition(pos, species, side, 0, 1, 5.0))
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds or done == 0:
+        distributed_energy_forces(model, layout, p, sp, src, dst, shift)
+        done += atoms
+    elapsed = time.perf_counter() - t0
+    return {"value": round(done / elapsed, 1), "unit": "atom-steps/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"{done} atom-steps of a {atoms}-atom system, E+F+virial of the same model "
+                                      f"on the oracle ops (torch CPU FP32), {elapsed:.1f} s"}
+
+
+def mace_train_cpu(seconds, atoms=128):
+    """configs[3] training step (C128/lmax3, force loss, Adam) on the oracle ops, torch CPU
+    FP32 with all host threads, on one small configuration: the port's CPU speed."""
+    from mace_ictc.models import MACEICTC
+    from oracle.model_ops import OracleOps
+    torch.set_num_threads(os.cpu_count() or 1)
+    pos, species, side, src, dst, shift = _cpu_system(atoms, 12)
+    torch.manual_seed(0)
+    model = MACEICTC(channels=128, lmax=3, num_interactions=2, correlation=3, r_max=5.0,
+                     avg_num_neighbors=src.numel() / atoms, ops=OracleOps(torch.float32))
+    opt = torch.optim.Adam([p for p in model.parameters() if p.requires_grad], lr=1e-3)
+    gen = torch.Generator().manual_seed(77)
+    e_target, f_target = torch.randn(1, generator=gen), torch.randn(atoms, 3, generator=gen)
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds or done == 0:
+        opt.zero_grad(set_to_none=True)
+        p = pos.detach().requires_grad_(True)
+        energy = model.energy(p, species, src, dst, shift)
+        (grad,) = torch.autograd.grad(energy.sum(), [p], create_graph=True)
+        loss = ((energy / atoms - e_target) ** 2).mean() + 100.0 * ((-grad - f_target) ** 2).mean()
+        loss.backward()
+        opt.step()
+        done += atoms
+    elapsed = time.perf_counter() - t0
+    return {"value": round(done / elapsed, 1), "unit": "atom-steps/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"{done} atom-steps of training on one {atoms}-atom configuration with the "
+                                      f"same model on the oracle ops (torch CPU FP32), {elapsed:.1f} s"}
+
+
+def mace_block_cpu(seconds, atoms=1024):
+    """The same block on the oracle ops (torch CPU FP32, all host threads), smaller system."""
+    from mace_ictc.models import InteractionBlock, ProductBlock, radial_embedding, species_groups
+    from oracle.model_ops import OracleOps
+    torch.set_num_threads(os.cpu_count() or 1)
+    pos, species, side, src, dst, shift = _cpu_system(atoms, 3)
     torch.manual_seed(0)
     C, L = 64, 2
     ops = OracleOps(torch.float32)
@@ -486,6 +543,14 @@ def mace_md(device, world, rank, steps, warmup, atoms=262144, cutoff=5.0, phases
     return result
 
 
+def arm_config(world):
+    """The workload description both arms report."""
+    return {"workload": WORKLOAD, "channels": C, "lmax": L, "paths": PATHS,
+            "instances_per_step": FWD_ROWS, "per_gpu_instances": FWD_ROWS, "layout": "ir_mul",
+            "l2": "inputs (7.3 GB) and output (13.3 GB) far exceed the 126 MB L2; no flush needed",
+            "parallelism": f"replicas x{world} (independent instances, no collective)"}
+
+
 def run_ours(args):
     world, rank, local = setup_dist()
     device = torch.device("cuda", local)
@@ -525,6 +590,9 @@ def run_ours(args):
     torch.cuda.empty_cache()
     train = mace_train(device, 3, 2) if world == 1 else None
     torch.cuda.empty_cache()
+    if world == 1 and rank == 0:
+        md["cpu_baseline"] = mace_md_cpu(args.cpu_seconds / 3)
+        train["cpu_baseline"] = mace_train_cpu(args.cpu_seconds / 3)
 
     e2e_steps = max(2, min(args.steps, 5))
     e2e_ms, h2d, d2h = e2e_forward(op, FWD_ROWS, e2e_steps, 1, device, world)
@@ -541,10 +609,7 @@ def run_ours(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(fwd_ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": round(value / PUBLISHED_FWD, 2),
         "dtype": "f32", "data": "synthetic (seeded; configs[1] distributions)",
-        "config": {"workload": WORKLOAD, "channels": C, "lmax": L, "paths": PATHS,
-                   "instances_per_step": FWD_ROWS, "per_gpu_instances": FWD_ROWS, "layout": "ir_mul",
-                   "l2": "inputs (7.3 GB) and output (13.3 GB) far exceed the 126 MB L2; no flush needed",
-                   "parallelism": f"replicas x{world} (independent instances, no collective)"},
+        "config": arm_config(world),
         "roofline": roofline(FWD_BYTES, FWD_ROWS, fwd_ms, profiled_traffic("tp_forward_c128_l3.txt")),
         "fwd_vjp": {"value": round(world * VJP_ROWS / (vjp_ms * 1e-3), 1), "unit": "TP instances/s",
                     "instances_per_step": VJP_ROWS, "ms_per_step": round(vjp_ms, 4),
@@ -585,8 +650,8 @@ def _cpu_tp_setup(rows, seed):
     return owner, blocks, harm, g.view(rows, PATHS, C), tp_oracle
 
 
-def cpu_baseline(seconds, rows=2048):
-    """Oracle port of the reference CPU TP forward, all host threads, bounded sample."""
+def cpu_baseline_port(seconds, rows=2048):
+    """Oracle port of the reference CPU TP forward (oracle/tp_oracle.py), all host threads."""
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     owner, blocks, harm, g, tp_oracle = _cpu_tp_setup(rows, 5)
@@ -602,21 +667,97 @@ def cpu_baseline(seconds, rows=2048):
                       f"(oracle/tp_oracle.py, torch CPU FP32, {elapsed:.1f} s)"}
 
 
+def cpu_baseline(seconds):
+    """The stock reference module timed in a child process (both packages are named
+    ``ictc_o3``, so the reference cannot be imported next to this one); the port as
+    a second, labelled number."""
+    port = cpu_baseline_port(seconds / 2)
+    steps = 4
+    proc = subprocess.run([sys.executable, os.path.abspath(__file__), "--impl", "reference", "--steps", str(steps),
+                           "--warmup", "1"], capture_output=True, text=True, timeout=600)
+    line = None
+    for text in proc.stdout.splitlines():
+        if text.startswith("{"):
+            line = json.loads(text)
+    if proc.returncode != 0 or line is None or "unavailable" in line:
+        port["note"] = "reference package unavailable: " + (line or {}).get("unavailable", proc.stderr[-300:])
+        return port
+    base = dict(line["cpu_baseline"])
+    base["port"] = port
+    return base
+
+
+REF_ROOT = os.path.join(REPO, "baseline", "_ref")
+REF_ROWS = 4096
+
+
+def _reference_package():
+    """Make ``ictc_o3`` resolve to the installed reference package (baseline/_ref) in
+    this process; False when it is not installed."""
+    if not os.path.isfile(os.path.join(REF_ROOT, "ictc_o3", "basis", "ictd_irreps.py")):
+        return False
+    if "ictc_o3" in sys.modules:
+        raise RuntimeError("this process already imported the backend's ictc_o3")
+    os.environ.setdefault("FSCETP_ICTD_CACHE", "0")        # no disk cache writes from the reference
+    while PACKAGE_ROOT in sys.path:
+        sys.path.remove(PACKAGE_ROOT)
+    sys.path.insert(0, REF_ROOT)
+    return True
+
+
+def _reference_tp(rows, seed):
+    """The reference's own module, built as its operator factory builds it
+    (``ictc_o3/operators.py:43-66``: operator paths, FP32, path weights fixed to 1),
+    on the configs[1] inputs (features N(0,1), harmonics of random unit vectors,
+    gates N(0, 1/sqrt(23)))."""
+    from ictc_o3.basis.ictd_irreps import EdgeWeightedPathPreservingTensorProduct, direction_harmonics_all
+    paths = [(i, j, k) for i in range(L + 1) for j in range(L + 1) for k in range(L + 1)
+             if abs(i - j) <= k <= i + j and (i + j + k) % 2 == 0]
+    tp = EdgeWeightedPathPreservingTensorProduct(channels=C, lmax=L, allowed_paths=paths,
+                                                 internal_compute_dtype=torch.float32)
+    with torch.no_grad():
+        tp.weight.fill_(1.0)
+    tp.weight.requires_grad_(False)
+    gen = torch.Generator().manual_seed(seed)
+    x = {l: torch.randn(rows, C, 2 * l + 1, generator=gen) for l in range(L + 1)}
+    n = torch.nn.functional.normalize(torch.randn(rows, 3, generator=gen), dim=1)
+    y = {l: h.unsqueeze(1) for l, h in enumerate(direction_harmonics_all(n, L))}
+    g = torch.randn(rows, GATE_W, generator=gen) / PATHS ** 0.5
+    return tp, x, y, g
+
+
 def run_reference(args):
+    """Reference arm: the stock ``EdgeWeightedPathPreservingTensorProduct.forward``
+    (``ictc_o3/basis/ictd_irreps.py:2750-2795``) from the installed reference package on
+    the host cores, each step a bounded sample of the configs[1] workload.  Without
+    the installed package, the oracle port (labelled "port")."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    rows = 2048
-    owner, blocks, harm, g, tp_oracle = _cpu_tp_setup(rows, 17)
+    if _reference_package():
+        rows = REF_ROWS
+        tp, x, y, g = _reference_tp(rows, 17)
+
+        def forward():
+            tp(x, y, g)
+        kind, what = "reference", ("stock ictc_o3 EdgeWeightedPathPreservingTensorProduct.forward "
+                                   "(baseline/_ref, torch CPU FP32)")
+    else:
+        rows = 2048
+        owner, blocks, harm, g, tp_oracle = _cpu_tp_setup(rows, 17)
+
+        def forward():
+            tp_oracle.tp_forward(owner, blocks, harm, g)
+        kind, what = "port", "oracle/tp_oracle.py port (reference package not installed)"
     with torch.no_grad():
         for _ in range(args.warmup):
-            tp_oracle.tp_forward(owner, blocks, harm, g)
+            forward()
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            tp_oracle.tp_forward(owner, blocks, harm, g)
+            forward()
         elapsed = time.perf_counter() - t0
     value = args.steps * rows / elapsed
     line = {
@@ -624,10 +765,9 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * elapsed / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": round(value / PUBLISHED_FWD, 6),
         "dtype": "f32", "data": "synthetic (seeded; configs[1] distributions)", "impl": "reference",
-        "config": {"workload": WORKLOAD, "channels": C, "lmax": L, "paths": PATHS,
-                   "instances_per_step": rows, "parallelism": "host CPU"},
-        "cpu_baseline": {"value": round(value, 1), "unit": "TP instances/s", "cores": threads, "kind": "port",
-                         "sample": f"each step = {rows} instances of the {FWD_ROWS}-instance workload"},
+        "config": arm_config(world),
+        "cpu_baseline": {"value": round(value, 1), "unit": "TP instances/s", "cores": threads, "kind": kind,
+                         "sample": f"each step = {rows} instances of the {FWD_ROWS}-instance workload; {what}"},
         "e2e": {"value": round(value, 1), "unit": "TP instances/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
