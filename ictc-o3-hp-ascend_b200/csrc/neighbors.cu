@@ -342,16 +342,25 @@ static std::mutex g_scratch_mutex;
 static void* g_scratch_address[kMaxDevices] = {};
 
 // Device address of g_neighbor_scratch on the current device (host code must not use
-// the symbol's host-side name as a device pointer).  Resolved once per device.
-static int scratch_address(void** out) {
+// the symbol's host-side name as a device pointer).  Looked up with the device current
+// on every call that is not being captured into a CUDA graph, so a context that was
+// torn down and re-created (cudaDeviceReset) never leaves a stale address behind;
+// captured calls use the address of the last uncaptured call on that device, and a
+// device's first call must therefore not be captured.
+static int scratch_address(cudaStream_t stream, void** out) {
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) {
     cudaGetLastError();
     ictc_set_error("ictc_neighbor_list_noalloc: no usable current device%s", "");
     return ICTC_ERR_CUDA;
   }
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &capture) != cudaSuccess) {
+    cudaGetLastError();
+    capture = cudaStreamCaptureStatusActive;  // unknown: do not call into the runtime's module table
+  }
   std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (!g_scratch_address[device]) {
+  if (capture == cudaStreamCaptureStatusNone) {
     void* ptr = nullptr;
     cudaError_t err = cudaGetSymbolAddress(&ptr, g_neighbor_scratch);
     if (err != cudaSuccess || !ptr) {
@@ -360,6 +369,9 @@ static int scratch_address(void** out) {
       return ICTC_ERR_CUDA;
     }
     g_scratch_address[device] = ptr;
+  } else if (!g_scratch_address[device]) {
+    ictc_set_error("ictc_neighbor_list_noalloc: the first call on a device must not be captured%s", "");
+    return ICTC_ERR_INVALID;
   }
   *out = g_scratch_address[device];
   return ICTC_OK;
@@ -430,7 +442,7 @@ extern "C" int ictc_neighbor_list_noalloc(const float* pos, int64_t atoms, const
     return ICTC_ERR_INVALID;
   }
   void* scratch = nullptr;
-  int status = scratch_address(&scratch);
+  int status = scratch_address((cudaStream_t)stream, &scratch);
   if (status != ICTC_OK) return status;
   status = ictc_neighbor_count(pos, atoms, box, cutoff, scratch, (int64_t)kNoAllocScratchBytes, offsets, stream);
   if (status != ICTC_OK || atoms == 0) return status;

@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, (LO >= 3) ? 1 : 2)
     // Two channels per lane leave no registers for the direct path's pipeline:
     // the host launches this width only with staged rows.
     if (!staged) {
-      if (threadIdx.x == 0 && a.status) atomicExch(a.status, 2);
+      if (threadIdx.x == 0 && a.status) atomicMax(a.status, 2);
       return;
     }
   }
@@ -304,9 +304,12 @@ __global__ void __launch_bounds__(kThreads, (LO >= 3) ? 1 : 2)
         if (!ok) {
           // Lost copy: record it, give the copies in flight a last bounded chance
           // to land (the buffers must not be written after the warp leaves), stop.
-          if (lane == 0 && a.status) atomicExch(a.status, 1);
-          tc::mbar_wait(s_bar + slot, (phases >> slot) & 1u, kStageWaitNs);
-          if (pending) tc::mbar_wait(s_bar + (slot ^ 1), (phases >> (slot ^ 1)) & 1u, kStageWaitNs);
+          // A drain that also times out means a copy may still write shared memory
+          // after this CTA exits: status 3, which the host treats as fatal.
+          if (lane == 0 && a.status) atomicMax(a.status, 1);
+          bool drained = tc::mbar_wait(s_bar + slot, (phases >> slot) & 1u, kStageWaitNs);
+          if (pending) drained = tc::mbar_wait(s_bar + (slot ^ 1), (phases >> (slot ^ 1)) & 1u, kStageWaitNs) && drained;
+          if (!drained && lane == 0 && a.status) atomicMax(a.status, 3);
           return;
         }
         phases ^= 1u << slot;
@@ -561,7 +564,7 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2)
   if constexpr (staged) {
     // Launched only with a staging buffer (one warp per node, aligned rows).
     if (a.stage_floats <= 0 || a.slices != 1) {
-      if (threadIdx.x == 0 && a.status) atomicExch(a.status, 2);
+      if (threadIdx.x == 0 && a.status) atomicMax(a.status, 2);
       return;
     }
   }
@@ -656,9 +659,11 @@ __global__ void __launch_bounds__(kThreads, (GRAPH && LI >= 3) ? 1 : 2)
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) {
             // Lost copy: record it, give the copy in flight a last bounded chance to
-            // land (the buffer must not be written after the warp leaves), and stop.
-            if (lane == 0 && a.status) atomicExch(a.status, 1);
-            tc::mbar_wait(s_bar, phase, kStageWaitNs);
+            // land (the buffer must not be written after the warp leaves), and stop;
+            // status 3 (fatal for the context) if that drain times out as well.
+            if (lane == 0 && a.status) atomicMax(a.status, 1);
+            const bool drained = tc::mbar_wait(s_bar, phase, kStageWaitNs);
+            if (!drained && lane == 0 && a.status) atomicMax(a.status, 3);
             return;
           }
           phase ^= 1u;

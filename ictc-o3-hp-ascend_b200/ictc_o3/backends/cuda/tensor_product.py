@@ -69,8 +69,16 @@ class TPPlan:
         return int(value.value)
 
     def check_status(self):
-        """Raise if a kernel of this plan recorded a timed-out wait."""
+        """Raise if a kernel of this plan recorded a timed-out wait.
+
+        Codes: 1 a staged copy did not land in time (the copies in flight drained;
+        the context stays usable), 2 a launch the kernel does not support, 3 a staged
+        copy did not land and neither did the drain: a bulk copy may still write
+        shared memory of a finished CTA, so the CUDA context must be considered lost."""
         code = self.status()
+        if code == 3:
+            raise RuntimeError("tensor-product kernel reported error 3: a staged copy never completed and its "
+                               "drain timed out; treat this CUDA context as lost (restart the process)")
         if code:
             raise RuntimeError(f"tensor-product kernel reported error {code} (timed-out staging wait)")
 

@@ -71,10 +71,15 @@ int ictc_tp_plan_destroy(ictc_tp_plan* plan);
 int ictc_tp_plan_info(const ictc_tp_plan* plan, int64_t* info, int n);
 
 /* Status word of the plan's kernels: *status = 0, or non-zero after a kernel
- * gave up on a timed-out wait (the graph adjoint's staged row copies); the
- * kernel then leaves its remaining work undone.  Reads one int from the device
- * (synchronising); reset != 0 clears the word.  No reference counterpart: the
- * reference backends have no asynchronous copies to lose. */
+ * gave up on a timed-out wait (the graph kernels' staged row copies); the
+ * kernel then leaves its remaining work undone.  1: a copy did not land in
+ * time and the copies in flight drained (the context stays usable); 2: a launch
+ * shape the kernel does not support; 3: a copy did not land and the drain timed
+ * out too, so a bulk copy may still write shared memory after its CTA ended --
+ * treat the CUDA context as lost.  The word keeps the largest code.  Reads one
+ * int from the device (synchronising); reset != 0 clears the word.  No
+ * reference counterpart: the reference backends have no asynchronous copies to
+ * lose. */
 int ictc_tp_plan_status(const ictc_tp_plan* plan, int32_t* status, int reset);
 
 /*
@@ -298,8 +303,10 @@ int ictc_wait_selftest(int* status, int64_t limit_ns, int arrive, void* stream);
  * edges are written only when that count is <= max_edges (read offsets[atoms]
  * after the stream completes to detect a too-small capacity).  Calls that
  * overlap on the GPU (other streams or threads) share the array and race;
- * serialise them.  The first call on a device resolves the array's device
- * address; make that first call before any stream capture.  Nothing is
+ * serialise them.  Every call made outside stream capture looks up the array's
+ * device address with that device current (so a context reset cannot leave a
+ * stale address); a captured call reuses the last address looked up on its
+ * device, so make a device's first call before any stream capture.  Nothing is
  * allocated or freed.
  */
 int64_t ictc_neighbor_noalloc_scratch_bytes(void);
