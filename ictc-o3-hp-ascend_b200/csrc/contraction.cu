@@ -287,9 +287,79 @@ static SCFn sc_kernel(int lmax, int corr, bool backward) {
   return nullptr;
 }
 
+// ---------------------------------------------------------------------------
+// Weight fold of one target degree: T[s, row0 + r, c] = sum_p U[r, p] W[s, p, c]
+// (U = symmetrised coupling rows [R, P], W = species weights [S, P, C], T rows of
+// stride t_rows).  A warp owns one output row r and 32 channels; U[r, :] is a
+// warp-uniform broadcast, W rows are coalesced over c.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) sc_fold_kernel(const float* __restrict__ U, const float* __restrict__ W,
+                                                      float* __restrict__ T, int R, int P, int C, int64_t t_rows,
+                                                      int64_t row0) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 8 + warp;
+  const int s = blockIdx.y;
+  const int c = blockIdx.z * 32 + lane;
+  if (r >= R || c >= C) return;
+  const float* u = U + (int64_t)r * P;
+  const float* w = W + (int64_t)s * P * C + c;
+  float acc = 0.f;
+  for (int p = 0; p < P; ++p) acc = fmaf(__ldg(u + p), __ldg(w + (int64_t)p * C), acc);
+  T[((int64_t)s * t_rows + row0 + r) * C + c] = acc;
+}
+
+// Adjoint of the fold: dW[s, p, c] = sum_r U[r, p] dT[s, row0 + r, c].  One block per
+// (p, s, 32 channels): its 8 warps take rows r = warp, warp + 8, ... and the partial
+// sums meet in shared memory in a fixed order (deterministic, no atomics).
+__global__ void __launch_bounds__(256) sc_fold_adjoint_kernel(const float* __restrict__ U,
+                                                              const float* __restrict__ dT, float* __restrict__ dW,
+                                                              int R, int P, int C, int64_t t_rows, int64_t row0) {
+  __shared__ float part[8][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int p = blockIdx.x, s = blockIdx.y, c = blockIdx.z * 32 + lane;
+  float acc = 0.f;
+  if (c < C) {
+    const float* g = dT + ((int64_t)s * t_rows + row0) * C + c;
+    for (int r = warp; r < R; r += 8) acc = fmaf(__ldg(U + (int64_t)r * P + p), __ldg(g + (int64_t)r * C), acc);
+  }
+  part[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && c < C) {
+    float total = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) total += part[k][lane];
+    dW[((int64_t)s * P + p) * C + c] = total;
+  }
+}
+
 }  // namespace ictc
 
 using namespace ictc;
+
+extern "C" int ictc_sc_fold(const float* usym, const float* weights, float* table, int rows, int cols,
+                            int channels, int species, int64_t table_rows, int64_t row0, int adjoint, void* stream) {
+  if (rows < 0 || cols < 0 || channels < 0 || species < 0 || row0 < 0 || row0 + rows > table_rows ||
+      ((int64_t)rows * cols * channels * species > 0 && (!usym || !weights || !table))) {
+    ictc_set_error("ictc_sc_fold: invalid argument%s", "");
+    return ICTC_ERR_INVALID;
+  }
+  if ((int64_t)rows * cols * channels * species == 0) return ICTC_OK;
+  const unsigned cz = (unsigned)((channels + 31) / 32);
+  if (adjoint) {
+    // weights <- dW [S, P, C]; table = dT [S, table_rows, C]
+    sc_fold_adjoint_kernel<<<dim3((unsigned)cols, (unsigned)species, cz), 256, 0, (cudaStream_t)stream>>>(
+        usym, table, const_cast<float*>(weights), rows, cols, channels, table_rows, row0);
+  } else {
+    sc_fold_kernel<<<dim3((unsigned)((rows + 7) / 8), (unsigned)species, cz), 256, 0, (cudaStream_t)stream>>>(
+        usym, weights, table, rows, cols, channels, table_rows, row0);
+  }
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) {
+    ictc_set_error("symmetric contraction fold launch failed: %s", cudaGetErrorString(err));
+    return ICTC_ERR_CUDA;
+  }
+  return ICTC_OK;
+}
 
 extern "C" int64_t ictc_sc_table_rows(int lmax, int correlation, int target_lmax) {
   if (lmax < 0 || correlation < 1 || correlation > 3 || target_lmax < 0) return -1;

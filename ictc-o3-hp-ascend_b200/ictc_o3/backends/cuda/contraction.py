@@ -256,14 +256,76 @@ def _table_gradient(tiles, tile_species, x, grad, shape, spec, chunk=256):
 # Entry point
 # ---------------------------------------------------------------------------
 
+class _Fold(torch.autograd.Function):
+    """T [S, sum_t R_t, C]: every target's block T_t = Usym_t W_t (``ictc_sc_fold``).
+
+    Linear in the weights: the weight gradient is the adjoint fold, whose own
+    derivative is the fold again, so derivatives of every order stay kernels."""
+
+    @staticmethod
+    def forward(ctx, usyms, rows, *weights):
+        ctx.usyms, ctx.rows = usyms, rows
+        S, C = weights[0].shape[0], weights[0].shape[2]
+        total = sum(rows)
+        table = torch.empty(S, total, C, device=weights[0].device, dtype=torch.float32)
+        row0, stream = 0, stream_of(weights[0])
+        for usym, w, r in zip(usyms, weights, rows):
+            w = w.contiguous()
+            _native.call("ictc_sc_fold", ptr(usym), ptr(w), ptr(table), int(r), int(w.shape[1]), int(C), int(S),
+                         int(total), int(row0), 0, stream)
+            row0 += r
+        ctx.shapes = [tuple(w.shape) for w in weights]
+        return table
+
+    @staticmethod
+    def backward(ctx, grad):
+        return (None, None) + tuple(_FoldAdjoint.apply(ctx.usyms, ctx.rows, ctx.shapes, grad.contiguous()))
+
+
+class _FoldAdjoint(torch.autograd.Function):
+    """dW_t [S, P_t, C] = Usym_t^T dT_t for every target block of dT."""
+
+    @staticmethod
+    def forward(ctx, usyms, rows, shapes, grad):
+        ctx.usyms, ctx.rows, ctx.shapes = usyms, rows, shapes
+        total, row0, stream = sum(rows), 0, stream_of(grad)
+        out = []
+        for usym, shape, r in zip(usyms, shapes, rows):
+            dw = torch.empty(shape, device=grad.device, dtype=torch.float32)
+            _native.call("ictc_sc_fold", ptr(usym), ptr(dw), ptr(grad), int(r), int(shape[1]), int(shape[2]),
+                         int(shape[0]), int(total), int(row0), 1, stream)
+            out.append(dw)
+            row0 += r
+        return tuple(out)
+
+    @staticmethod
+    def backward(ctx, *grads):
+        grads = [torch.zeros(shape, device=ctx.usyms[0].device) if g is None else g.contiguous()
+                 for g, shape in zip(grads, ctx.shapes)]
+        return None, None, None, _Fold.apply(ctx.usyms, ctx.rows, *grads)
+
+
 def coefficient_table(owner, device):
-    """T [S, R, C] = Usym W for all targets (differentiable in the weights)."""
-    parts = []
-    for contraction in owner.contractions:
-        weights = contraction.stacked_weights()                       # [S, P, C]
-        usym = contraction.symmetric_table(device, weights.dtype)     # [rows*M, P]
-        parts.append(torch.matmul(usym.unsqueeze(0), weights))        # [S, rows*M, C]
-    return torch.cat(parts, 1).contiguous()
+    """T [S, R, C] = Usym W for all targets, folded by ``ictc_sc_fold``.
+
+    Differentiable in the weights.  When no weight needs a gradient (frozen weights,
+    or gradients disabled), the folded table is kept and reused until a weight
+    changes (same tensors and versions)."""
+    weights = [c.stacked_weights() for c in owner.contractions]                 # [S, P_t, C] each
+    usyms = tuple(c.symmetric_table(device, torch.float32) for c in owner.contractions)
+    rows = tuple(int(u.shape[0]) for u in usyms)
+    params = [p for c in owner.contractions for p in c.parameters()]
+    live = torch.is_grad_enabled() and any(p.requires_grad for p in params)
+    if live:
+        return _Fold.apply(usyms, rows, *weights)
+    key = (str(device), tuple((p.data_ptr(), p._version) for p in params))
+    cached = owner.__dict__.get("_cuda_folded_table")
+    if cached is not None and cached[0] == key:
+        return cached[1]
+    with torch.no_grad():
+        table = _Fold.apply(usyms, rows, *[w.detach() for w in weights])
+    owner.__dict__["_cuda_folded_table"] = (key, table)
+    return table
 
 
 def contract_flat(owner, node_feats: torch.Tensor, index: torch.Tensor) -> torch.Tensor:

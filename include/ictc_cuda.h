@@ -191,6 +191,17 @@ int ictc_edge_geometry_backward(const float* vec, const float* grad_unit, const 
  * (ictc_o3/ops/_mace_symmetric_contraction.py:298-346) and the Ascend factorised
  * contraction (ictc_o3/backends/ascend/contraction.py:8-45).
  */
+/* Weight fold of one target degree of the symmetric contraction (replaces the
+ * species-bank projection of backends/ascend/contraction.py:8-45, the dense GEMM
+ * that folds the weights into the coupling constants):
+ *   adjoint = 0: table[s, row0 + r, c] = sum_p usym[r, p] * weights[s, p, c]
+ *   adjoint = 1: weights[s, p, c] = sum_r usym[r, p] * table[s, row0 + r, c]
+ *                (the weight gradient: table holds dT, weights receives dW)
+ * usym [rows, cols] (symmetrised couplings, rows = monomials x (2t+1)),
+ * weights [species, cols, channels], table [species, table_rows, channels].
+ * Deterministic (no atomics). */
+int ictc_sc_fold(const float* usym, const float* weights, float* table, int rows, int cols, int channels,
+                 int species, int64_t table_rows, int64_t row0, int adjoint, void* stream);
 int64_t ictc_sc_table_rows(int lmax, int correlation, int target_lmax);
 int ictc_sc_tile_nodes(void);
 int ictc_sc_forward(const float* x, const float* table, const int64_t* tiles, const int32_t* tile_species,

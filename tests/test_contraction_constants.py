@@ -80,7 +80,7 @@ def test_symmetric_table_reproduces_the_polynomial():
 def test_second_order_polynomial_matches_oracle(lmax, target, corr):
     """The differentiable polynomial of the second-order path equals the recursion,
     and so do its first and mixed second derivatives (FP64, CPU)."""
-    from ictc_o3.backends.cuda.contraction import coefficient_table, polynomial, species_tiles
+    from ictc_o3.backends.cuda.contraction import polynomial, species_tiles
     from ictc_o3.ops.symmetric_contraction import ICTDPureUSymmetricContractionSO3
     torch.manual_seed(3)
     S, N, C = 3, 13, 4
@@ -88,7 +88,9 @@ def test_second_order_polynomial_matches_oracle(lmax, target, corr):
                                               correlation=corr).double()
     x = torch.randn(N, C * (lmax + 1) ** 2, dtype=torch.float64, requires_grad=True)
     idx = torch.randint(0, S, (N,))
-    table = coefficient_table(module, torch.device("cpu"))
+    # the folded table T_t = Usym_t W_t in FP64 (the kernels fold it on the GPU)
+    table = torch.cat([torch.matmul(c.symmetric_table(torch.device("cpu"), torch.float64).unsqueeze(0),
+                                    c.stacked_weights()) for c in module.contractions], 1)
     tiles, tile_species = species_tiles(idx, S)
     out = polynomial(x, table.double(), tiles, tile_species, (C, lmax, corr, target))
     feats = sc_oracle.flat_to_mace(x, C, lmax)

@@ -106,3 +106,45 @@ def test_contraction_second_derivatives_against_oracle(lmax, target, corr, cuda_
     assert_close(dx.detach().cpu(), rdx.detach(), 1e-4, 1e-3, "dx")
     for k, (a, b) in enumerate(zip(got, want)):
         assert_close(a.cpu(), b, 1e-4, 1e-3, f"second derivative {k}")
+
+
+def _ref_fold(module, params, device):
+    """The folded table in FP64 torch from (FP64 CPU copies of) the module's weights."""
+    k, parts = 0, []
+    for c in module.contractions:
+        n = len(list(c.parameters()))
+        w = torch.cat(params[k:k + n], 1)
+        parts.append(torch.matmul(c.symmetric_table(device, torch.float64).cpu().unsqueeze(0), w))
+        k += n
+    return torch.cat(parts, 1)
+
+
+def test_weight_fold_kernel_and_its_derivatives(cuda_device):
+    """ictc_sc_fold: T_t = Usym_t W_t and dW_t = Usym_t^T dT_t against FP64 torch, the
+    second-order path through the adjoint, and the frozen-weight cache."""
+    from ictc_o3.backends.cuda.contraction import coefficient_table
+    from ictc_o3.ops.symmetric_contraction import ICTDPureUSymmetricContractionSO3
+    torch.manual_seed(7)
+    module = ICTDPureUSymmetricContractionSO3(num_elements=3, channels=40, lmax=2, target_lmax=2,
+                                              correlation=3).to(cuda_device)
+    params = list(module.parameters())
+    ref_params = [p.detach().double().cpu().requires_grad_(True) for p in params]
+    table = coefficient_table(module, cuda_device)
+    ref_table = _ref_fold(module, ref_params, cuda_device)
+    assert_close(table.detach().cpu(), ref_table.detach(), 1e-6, what="fold")
+    G = torch.randn(table.shape, device=cuda_device, requires_grad=True)
+    grads = torch.autograd.grad(table, params, G, create_graph=True)
+    ref_grads = torch.autograd.grad(ref_table, ref_params, G.detach().double().cpu())
+    for g, r in zip(grads, ref_grads):
+        assert_close(g.detach().cpu(), r, 1e-5, what="dW")
+    # second order: <dW(G), V> is linear in G; its G-gradient is the fold of V
+    V = [torch.randn_like(g) for g in grads]
+    (dG,) = torch.autograd.grad(sum((g * v).sum() for g, v in zip(grads, V)), [G])
+    assert_close(dG.cpu(), _ref_fold(module, [v.double().cpu() for v in V], cuda_device), 1e-5, what="d2")
+    # frozen weights: the folded table is kept until a weight changes
+    with torch.no_grad():
+        first = coefficient_table(module, cuda_device)
+        assert coefficient_table(module, cuda_device) is first
+        module.contractions[0].weights_max.add_(1.0)
+        again = coefficient_table(module, cuda_device)
+    assert again is not first and not torch.equal(again, first)
