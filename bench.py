@@ -177,6 +177,13 @@ def profiled_traffic(name):
     return None
 
 
+def vjp_traffic():
+    """DRAM bytes per instance of one forward + one fused adjoint launch (committed ncu
+    summaries of the two kernels), or None."""
+    fwd, adj = profiled_traffic("tp_forward_c128_l3.txt"), profiled_traffic("tp_adjoint_c128_l3.txt")
+    return None if fwd is None or adj is None else fwd + adj
+
+
 def roofline(bytes_per_inst, rows, kernel_ms, traffic_per_inst):
     peak, kind = peaks()
     achieved = bytes_per_inst * rows / (kernel_ms * 1e-3) / 1e9
@@ -613,7 +620,7 @@ def run_ours(args):
         "roofline": roofline(FWD_BYTES, FWD_ROWS, fwd_ms, profiled_traffic("tp_forward_c128_l3.txt")),
         "fwd_vjp": {"value": round(world * VJP_ROWS / (vjp_ms * 1e-3), 1), "unit": "TP instances/s",
                     "instances_per_step": VJP_ROWS, "ms_per_step": round(vjp_ms, 4),
-                    "roofline": roofline(VJP_BYTES, VJP_ROWS, vjp_ms, None),
+                    "roofline": roofline(VJP_BYTES, VJP_ROWS, vjp_ms, vjp_traffic()),
                     "gpu_launches_per_step": 2},
         "e2e": {"value": round(world * FWD_ROWS / (e2e_ms * 1e-3), 1), "unit": "TP instances/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

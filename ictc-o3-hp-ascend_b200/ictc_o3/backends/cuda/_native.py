@@ -33,6 +33,9 @@ _SIGNATURES = {
     "ictc_harmonics_table_size": [_i],
     "ictc_sc_table_rows": [_i, _i, _i],
     "ictc_sc_fold": [_p, _p, _p, _i, _i, _i, _i, _i64, _i64, _i, _p],
+    "ictc_sc_directional": [_p, _p, _p, _p, _p, _i64, _p, _i, _i, _i, _i, _p],
+    "ictc_sc_hvp": [_p, _p, _p, _p, _p, _i64, _p, _p, _i, _i, _i, _i, _p],
+    "ictc_sc_table_grad": [_p, _p, _p, _p, _p, _i64, _p, _i, _i, _i, _i, _i, _p],
     "ictc_sc_tile_nodes": [],
     "ictc_sc_forward": [_p, _p, _p, _p, _i64, _p, _i, _i, _i, _i, _p],
     "ictc_sc_backward": [_p, _p, _p, _p, _i64, _p, _p, _i, _i, _i, _i, _p],

@@ -103,39 +103,125 @@ def species_tiles(index: torch.Tensor, num_elements: int):
 # Autograd
 # ---------------------------------------------------------------------------
 
+def _sc_apply(name, spec, tiles, tile_species, x, table, grad=None, direction=None):
+    """One launch of a polynomial kernel over the species tiles.
+
+    ``ictc_sc_forward`` / ``ictc_sc_directional`` return [N, C sum_t M_t];
+    ``ictc_sc_backward`` / ``ictc_sc_hvp`` return [N, C D]; unnamed rows are zero."""
+    channels, lmax, correlation, target_lmax = spec
+    forward_like = name in ("ictc_sc_forward", "ictc_sc_directional")
+    width = channels * (target_lmax + 1) ** 2 if forward_like else x.shape[1]
+    out = torch.zeros(x.shape[0], width, device=x.device, dtype=torch.float32)
+    if tiles.shape[0]:
+        n = int(tiles.shape[0])
+        table = table.contiguous()
+        stream = stream_of(x)
+        if name == "ictc_sc_forward":
+            _native.call(name, ptr(x), ptr(table), ptr(tiles), ptr(tile_species), n, ptr(out), channels, lmax,
+                         correlation, target_lmax, stream)
+        elif name == "ictc_sc_backward":
+            _native.call(name, ptr(x), ptr(table), ptr(tiles), ptr(tile_species), n, ptr(grad), ptr(out), channels,
+                         lmax, correlation, target_lmax, stream)
+        elif name == "ictc_sc_directional":
+            _native.call(name, ptr(x), ptr(direction), ptr(table), ptr(tiles), ptr(tile_species), n, ptr(out),
+                         channels, lmax, correlation, target_lmax, stream)
+        else:
+            _native.call(name, ptr(x), ptr(direction), ptr(table), ptr(tiles), ptr(tile_species), n, ptr(grad),
+                         ptr(out), channels, lmax, correlation, target_lmax, stream)
+    return out
+
+
+def _sc_table_grad(spec, tiles, tile_species, x, grad, shape, direction=None):
+    """dT [S, R, C]: sum over each species' nodes of grad x monomials (directional
+    monomials along ``direction`` when given), ``ictc_sc_table_grad``."""
+    channels, lmax, correlation, target_lmax = spec
+    out = torch.empty(shape, device=x.device, dtype=torch.float32)
+    _native.call("ictc_sc_table_grad", ptr(x), ptr(direction), ptr(grad), ptr(tiles), ptr(tile_species),
+                 int(tiles.shape[0]), ptr(out), int(shape[0]), channels, lmax, correlation, target_lmax,
+                 stream_of(x))
+    return out
+
+
 class _Contraction(torch.autograd.Function):
     """out = poly(x; T) for species tiles; x [N, C*D] mul_ir flat, T [S, R, C]."""
 
     @staticmethod
     def forward(ctx, spec, tiles, tile_species, x, table):
-        channels, lmax, correlation, target_lmax = spec
         ctx.spec = spec
         ctx.save_for_backward(tiles, tile_species, x, table)
-        out = torch.zeros(x.shape[0], channels * (target_lmax + 1) ** 2, device=x.device, dtype=torch.float32)
-        if tiles.shape[0]:
-            _native.call("ictc_sc_forward", ptr(x), ptr(table), ptr(tiles), ptr(tile_species), int(tiles.shape[0]),
-                         ptr(out), channels, lmax, correlation, target_lmax, stream_of(x))
-        return out
+        return _sc_apply("ictc_sc_forward", spec, tiles, tile_species, x, table)
 
     @staticmethod
     def backward(ctx, grad):
         tiles, tile_species, x, table = ctx.saved_tensors
-        channels, lmax, correlation, target_lmax = ctx.spec
         need = required_gradients((x, table), ctx.needs_input_grad[3:5])
-        if torch.is_grad_enabled():
-            return (None, None, None) + _differentiable_gradients(tiles, tile_species, x, table, grad, ctx.spec,
-                                                                  need)
+        if not any(need):
+            return None, None, None, None, None
         grad = grad.contiguous()
-        dx = dtable = None
-        if need[0]:
-            dx = torch.zeros_like(x)
-            if tiles.shape[0]:
-                _native.call("ictc_sc_backward", ptr(x), ptr(table), ptr(tiles), ptr(tile_species),
-                             int(tiles.shape[0]), ptr(grad), ptr(dx), channels, lmax, correlation, target_lmax,
-                             stream_of(x))
-        if need[1]:
-            dtable = _table_gradient(tiles, tile_species, x, grad, table.shape, ctx.spec)
+        if torch.is_grad_enabled():
+            # The gradient itself will be differentiated (force-loss training): a
+            # kernel-backed function whose backward is again kernels.
+            dx, dtable = _ContractionGrad.apply(ctx.spec, tiles, tile_species, need, x, table, grad)
+            return None, None, None, dx, dtable
+        dx = _sc_apply("ictc_sc_backward", ctx.spec, tiles, tile_species, x, table, grad) if need[0] else None
+        dtable = _sc_table_grad(ctx.spec, tiles, tile_species, x, grad, table.shape) if need[1] else None
         return None, None, None, dx, dtable
+
+
+class _ContractionGrad(torch.autograd.Function):
+    """(dx, dT) of the polynomial for the output cotangent g, as kernels:
+        dx = sc_backward(x; T, g),   dT = table_grad(x, g).
+    Its derivatives, for cotangents hx on dx and hT on dT:
+        d/dg = directional(x, hx; T) + forward(x; hT)
+        d/dx = hvp(x, hx; T, g)      + backward(x; hT, g)
+        d/dT = table_grad(x, g, direction hx)
+    Differentiating once more (third order) recomputes through the torch
+    formulation of the polynomial."""
+
+    @staticmethod
+    def forward(ctx, spec, tiles, tile_species, need, x, table, grad):
+        ctx.spec, ctx.need = spec, need
+        ctx.save_for_backward(tiles, tile_species, x, table, grad)
+        dx = _sc_apply("ictc_sc_backward", spec, tiles, tile_species, x, table, grad) if need[0] else None
+        dtable = _sc_table_grad(spec, tiles, tile_species, x, grad, table.shape) if need[1] else None
+        return dx, dtable
+
+    @staticmethod
+    def backward(ctx, hx, htable):
+        tiles, tile_species, x, table, grad = ctx.saved_tensors
+        spec = ctx.spec
+        want = required_gradients((x, table, grad), ctx.needs_input_grad[4:7])
+        if not any(want) or (hx is None and htable is None):
+            return (None,) * 7
+        if torch.is_grad_enabled():
+            with torch.enable_grad():
+                xs, ts, gs = (t.detach().requires_grad_(True) for t in (x, table, grad))
+                dx, dt = _differentiable_gradients(tiles, tile_species, xs, ts, gs, spec, ctx.need)
+                outs = [(o, h) for o, h in ((dx, hx), (dt, htable)) if o is not None and h is not None]
+                got = list(torch.autograd.grad([o for o, _ in outs], [t for t, w in zip((xs, ts, gs), want) if w],
+                                               [h for _, h in outs], create_graph=True, allow_unused=True))
+            res = [got.pop(0) if w else None for w in want]
+            return (None, None, None, None, *res)
+        hx = None if hx is None else hx.contiguous()
+        htable = None if htable is None else htable.contiguous()
+        gx = gt = gg = None
+        if want[0]:
+            parts = []
+            if hx is not None:
+                parts.append(_sc_apply("ictc_sc_hvp", spec, tiles, tile_species, x, table, grad, hx))
+            if htable is not None:
+                parts.append(_sc_apply("ictc_sc_backward", spec, tiles, tile_species, x, htable, grad))
+            gx = sum(parts[1:], parts[0]) if parts else None
+        if want[1] and hx is not None:
+            gt = _sc_table_grad(spec, tiles, tile_species, x, grad, table.shape, direction=hx)
+        if want[2]:
+            parts = []
+            if hx is not None:
+                parts.append(_sc_apply("ictc_sc_directional", spec, tiles, tile_species, x, table, direction=hx))
+            if htable is not None:
+                parts.append(_sc_apply("ictc_sc_forward", spec, tiles, tile_species, x, htable))
+            gg = sum(parts[1:], parts[0]) if parts else None
+        return None, None, None, None, gx, gt, gg
 
 
 def _monomial_factors(dim: int, correlation: int, device):
@@ -212,44 +298,6 @@ def _differentiable_gradients(tiles, tile_species, x, table, grad, spec, need):
         g = grads.pop(0) if wanted else None
         result.append(torch.zeros_like(t) if wanted and g is None else g)
     return tuple(result)
-
-
-def _table_gradient(tiles, tile_species, x, grad, shape, spec, chunk=256):
-    """dT[s, row*M + m, c] = sum_{n of species s} G_t[n, c, m] x^{row}[n, c].
-
-    Weight-gradient path (training only), evaluated with batched GEMMs on the
-    device, species by species and in node chunks to bound memory.
-    """
-    channels, lmax, correlation, target_lmax = spec
-    dim = (lmax + 1) ** 2
-    rows = monomial_rows(dim, correlation)
-    n = x.shape[0]
-    feats = torch.cat([x[:, l * l * channels:(l + 1) ** 2 * channels].reshape(n, channels, 2 * l + 1)
-                       for l in range(lmax + 1)], -1)  # [N, C, D]
-    factors = [torch.tensor([mono[a] if a < len(mono) else -1 for mono in rows], device=x.device)
-               for a in range(correlation)]
-    dtable = torch.zeros(shape, device=x.device, dtype=torch.float32)
-    species = tile_species.to(torch.int64)
-    for s in torch.unique(species).tolist():
-        nodes = tiles[species == s].reshape(-1)
-        nodes = nodes[nodes >= 0]
-        for begin in range(0, nodes.numel(), chunk):
-            idx = nodes[begin:begin + chunk]
-            f = feats[idx]                                            # [n, C, D]
-            f1 = torch.cat([f, torch.ones_like(f[:, :, :1])], -1)     # index -1 -> 1
-            mono = torch.ones(idx.numel(), channels, len(rows), device=x.device)
-            for a in range(correlation):
-                mono = mono * f1[:, :, factors[a]]
-            mono_t = mono.permute(1, 2, 0)                            # [C, rows, n]
-            col, row_offset = 0, 0
-            for t in range(target_lmax + 1):
-                M = 2 * t + 1
-                g = grad[idx, col:col + channels * M].reshape(-1, channels, M).permute(1, 0, 2)  # [C, n, M]
-                part = torch.bmm(mono_t, g)                           # [C, rows, M]
-                dtable[s, row_offset:row_offset + len(rows) * M] += part.reshape(channels, -1).t()
-                col += channels * M
-                row_offset += len(rows) * M
-    return dtable
 
 
 # ---------------------------------------------------------------------------

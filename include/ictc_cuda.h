@@ -180,7 +180,7 @@ int ictc_edge_geometry_backward(const float* vec, const float* grad_unit, const 
  * MACE symmetric contraction as a per-node polynomial (correlation 1..3,
  * input degrees 0..lmax with 1 <= lmax <= 3, targets 0..target_lmax <= lmax).
  *   x      [N, C*(lmax+1)^2]   node features, degree blocks [C][2l+1] (mul_ir)
- *   table  [S, R, C]           species coefficient table T = Usym * W (host GEMM):
+ *   table  [S, R, C]           species coefficient table T = Usym * W (ictc_sc_fold):
  *          for each target t, monomial rows in the order
  *          for i: (i); for j >= i: (i,j); for k >= j: (i,j,k)   (orders <= correlation)
  *          each row holding 2t+1 consecutive C-vectors; R = ictc_sc_table_rows(...)
@@ -191,17 +191,6 @@ int ictc_edge_geometry_backward(const float* vec, const float* grad_unit, const 
  * (ictc_o3/ops/_mace_symmetric_contraction.py:298-346) and the Ascend factorised
  * contraction (ictc_o3/backends/ascend/contraction.py:8-45).
  */
-/* Weight fold of one target degree of the symmetric contraction (replaces the
- * species-bank projection of backends/ascend/contraction.py:8-45, the dense GEMM
- * that folds the weights into the coupling constants):
- *   adjoint = 0: table[s, row0 + r, c] = sum_p usym[r, p] * weights[s, p, c]
- *   adjoint = 1: weights[s, p, c] = sum_r usym[r, p] * table[s, row0 + r, c]
- *                (the weight gradient: table holds dT, weights receives dW)
- * usym [rows, cols] (symmetrised couplings, rows = monomials x (2t+1)),
- * weights [species, cols, channels], table [species, table_rows, channels].
- * Deterministic (no atomics). */
-int ictc_sc_fold(const float* usym, const float* weights, float* table, int rows, int cols, int channels,
-                 int species, int64_t table_rows, int64_t row0, int adjoint, void* stream);
 int64_t ictc_sc_table_rows(int lmax, int correlation, int target_lmax);
 int ictc_sc_tile_nodes(void);
 int ictc_sc_forward(const float* x, const float* table, const int64_t* tiles, const int32_t* tile_species,
@@ -213,6 +202,41 @@ int ictc_sc_forward(const float* x, const float* table, const int64_t* tiles, co
 int ictc_sc_backward(const float* x, const float* table, const int64_t* tiles, const int32_t* tile_species,
                      int64_t num_tiles, const float* grad_out, float* grad_x, int channels, int lmax,
                      int correlation, int target_lmax, void* stream);
+
+/* Weight fold of one target degree of the symmetric contraction (replaces the
+ * species-bank projection of backends/ascend/contraction.py:8-45, the dense GEMM
+ * that folds the weights into the coupling constants):
+ *   adjoint = 0: table[s, row0 + r, c] = sum_p usym[r, p] * weights[s, p, c]
+ *   adjoint = 1: weights[s, p, c] = sum_r usym[r, p] * table[s, row0 + r, c]
+ *                (the weight gradient: table holds dT, weights receives dW)
+ * usym [rows, cols] (symmetrised couplings, rows = monomials x (2t+1)),
+ * weights [species, cols, channels], table [species, table_rows, channels].
+ * Deterministic (no atomics). */
+int ictc_sc_fold(const float* usym, const float* weights, float* table, int rows, int cols, int channels,
+                 int species, int64_t table_rows, int64_t row0, int adjoint, void* stream);
+
+/* Second derivatives of ictc_sc_forward (force-loss training; no reference kernel:
+ * the reference differentiates its recursion with autograd,
+ * ictc_o3/backends/ascend/sparse_product.py:226-264).  dir [N, C*(lmax+1)^2] is a
+ * direction h in feature space; with the directional monomials (h.grad) mono(x):
+ *   ictc_sc_directional: out[n] = sum_r T[r] (h.grad) mono_r(x)  (derivative of the
+ *                        feature gradient with respect to the output cotangent)
+ *   ictc_sc_hvp:         grad_x[n] = gradient in x of sum_m grad_out[m] (h.grad) out[m]
+ *                        (Hessian-vector product of the polynomial)
+ *   ictc_sc_table_grad:  grad_table[s, row, c] = sum_{n of species s} grad_out[n] * v_row(n)
+ *                        with v = mono(x), or (h.grad) mono(x) when dir != NULL;
+ *                        tiles must list the species in ascending order (as the host
+ *                        builds them); every [species, row, channel] entry is written.
+ * Deterministic (no atomics). */
+int ictc_sc_directional(const float* x, const float* dir, const float* table, const int64_t* tiles,
+                        const int32_t* tile_species, int64_t num_tiles, float* out, int channels, int lmax,
+                        int correlation, int target_lmax, void* stream);
+int ictc_sc_hvp(const float* x, const float* dir, const float* table, const int64_t* tiles,
+                const int32_t* tile_species, int64_t num_tiles, const float* grad_out, float* grad_x, int channels,
+                int lmax, int correlation, int target_lmax, void* stream);
+int ictc_sc_table_grad(const float* x, const float* dir, const float* grad_out, const int64_t* tiles,
+                       const int32_t* tile_species, int64_t num_tiles, float* grad_table, int species, int channels,
+                       int lmax, int correlation, int target_lmax, void* stream);
 
 /*
  * Periodic cell-list neighbour search (orthorhombic box, cutoff < L/2, >= 3

@@ -148,3 +148,52 @@ def test_weight_fold_kernel_and_its_derivatives(cuda_device):
         module.contractions[0].weights_max.add_(1.0)
         again = coefficient_table(module, cuda_device)
     assert again is not first and not torch.equal(again, first)
+
+
+@pytest.mark.parametrize("lmax,target,corr,channels", [(2, 2, 3, 40), (3, 1, 3, 32), (1, 1, 2, 16), (2, 0, 3, 64)])
+def test_second_order_kernels(lmax, target, corr, channels, cuda_device):
+    """Force-loss training derivatives of the contraction through the kernels
+    (directional polynomial, Hessian-vector product, table gradients) against the
+    FP64 torch polynomial: dx, then the gradients of <dx, V> with respect to x, the
+    output cotangent G and the weights, and the first-order weight gradient."""
+    from ictc_o3.backends.cuda.contraction import contract_flat, polynomial, species_tiles
+    from ictc_o3.ops.symmetric_contraction import ICTDPureUSymmetricContractionSO3
+    torch.manual_seed(lmax * 10 + target)
+    S, N = 3, 203
+    module = ICTDPureUSymmetricContractionSO3(num_elements=S, channels=channels, lmax=lmax, target_lmax=target,
+                                              correlation=corr).to(cuda_device)
+    D = (lmax + 1) ** 2
+    x = (0.7 * torch.randn(N, channels * D, device=cuda_device)).requires_grad_(True)
+    idx = torch.randint(0, S, (N,), device=cuda_device)
+    params = list(module.parameters())
+    out = contract_flat(module, x, idx)
+    G = torch.randn(out.shape, device=cuda_device, requires_grad=True)
+    (dx,) = torch.autograd.grad(out, [x], G, create_graph=True)
+    V = torch.randn_like(dx)
+    hx, hG, *hW = torch.autograd.grad((dx * V).sum(), [x, G] + params, allow_unused=True)
+    (w1,) = torch.autograd.grad((out * G).sum(), [params[0]])            # first-order weight gradient
+
+    # FP64 reference: the same polynomial in torch, the same folded weights
+    spec = (channels, lmax, corr, target)
+    tiles, tile_species = species_tiles(idx, S)
+    p64 = [p.detach().double().requires_grad_(True) for p in params]
+    parts, k = [], 0
+    for c in module.contractions:
+        n = len(list(c.parameters()))
+        parts.append(torch.matmul(c.symmetric_table(cuda_device, torch.float64).unsqueeze(0),
+                                  torch.cat(p64[k:k + n], 1)))
+        k += n
+    table64 = torch.cat(parts, 1)
+    x64 = x.detach().double().requires_grad_(True)
+    G64 = G.detach().double().requires_grad_(True)
+    ref = polynomial(x64, table64, tiles, tile_species, spec)
+    assert_close(out.detach(), ref.detach(), 1e-5, what="forward")
+    (rdx,) = torch.autograd.grad(ref, [x64], G64, create_graph=True)
+    assert_close(dx.detach(), rdx.detach(), 1e-4, what="dx")
+    rhx, rhG, *rhW = torch.autograd.grad((rdx * V.double()).sum(), [x64, G64] + p64, allow_unused=True)
+    assert_close(hx, rhx, 1e-4, what="d<dx,V>/dx (Hessian-vector)")
+    assert_close(hG, rhG, 1e-4, what="d<dx,V>/dG (directional)")
+    for a, b in zip(hW, rhW):
+        assert_close(a, b, 1e-4, what="d<dx,V>/dW (directional table gradient)")
+    (rw1,) = torch.autograd.grad((ref * G64).sum(), [p64[0]])
+    assert_close(w1, rw1, 1e-4, what="dW (table gradient)")
