@@ -168,10 +168,10 @@ def test_second_order_kernels(lmax, target, corr, channels, cuda_device):
     params = list(module.parameters())
     out = contract_flat(module, x, idx)
     G = torch.randn(out.shape, device=cuda_device, requires_grad=True)
+    (w1,) = torch.autograd.grad(out, [params[0]], G.detach(), retain_graph=True)   # first-order weight gradient
     (dx,) = torch.autograd.grad(out, [x], G, create_graph=True)
     V = torch.randn_like(dx)
     hx, hG, *hW = torch.autograd.grad((dx * V).sum(), [x, G] + params, allow_unused=True)
-    (w1,) = torch.autograd.grad((out * G).sum(), [params[0]])            # first-order weight gradient
 
     # FP64 reference: the same polynomial in torch, the same folded weights
     spec = (channels, lmax, corr, target)
