@@ -112,7 +112,9 @@ def _sc_apply(name, spec, tiles, tile_species, x, table, grad=None, direction=No
     forward_like = name in ("ictc_sc_forward", "ictc_sc_directional")
     width = channels * (target_lmax + 1) ** 2 if forward_like else x.shape[1]
     out = torch.zeros(x.shape[0], width, device=x.device, dtype=torch.float32)
-    if tiles.shape[0]:
+    # No nodes (a rank that owns no atoms): nothing to launch.  The species tiles are
+    # never empty (they are padded per species), but an empty tensor has no storage.
+    if tiles.shape[0] and x.shape[0]:
         n = int(tiles.shape[0])
         table = table.contiguous()
         stream = stream_of(x)
@@ -135,6 +137,8 @@ def _sc_table_grad(spec, tiles, tile_species, x, grad, shape, direction=None):
     """dT [S, R, C]: sum over each species' nodes of grad x monomials (directional
     monomials along ``direction`` when given), ``ictc_sc_table_grad``."""
     channels, lmax, correlation, target_lmax = spec
+    if x.shape[0] == 0:                                   # no nodes: the sum over them is zero
+        return torch.zeros(shape, device=x.device, dtype=torch.float32)
     out = torch.empty(shape, device=x.device, dtype=torch.float32)
     _native.call("ictc_sc_table_grad", ptr(x), ptr(direction), ptr(grad), ptr(tiles), ptr(tile_species),
                  int(tiles.shape[0]), ptr(out), int(shape[0]), channels, lmax, correlation, target_lmax,

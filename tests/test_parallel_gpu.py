@@ -92,6 +92,29 @@ def _free_port():
         return sock.getsockname()[1]
 
 
+def _run_ranks(worker, args, world, deadline_s=300.0):
+    """Start ``world`` rank processes and wait for them with a deadline.
+
+    If a rank fails, the others can be left waiting for it inside NCCL; they are
+    then ended with SIGKILL (only the processes started here) so that the test fails
+    promptly instead of waiting for ever."""
+    import signal
+    import time
+    ctx = mp.start_processes(worker, args=args, nprocs=world, join=False, start_method="spawn")
+    start = time.time()
+    try:
+        while not ctx.join(timeout=5):
+            if time.time() - start > deadline_s:
+                raise TimeoutError(f"ranks did not finish within {deadline_s:.0f} s")
+    except BaseException:
+        for pid in ctx.pids():
+            try:
+                os.kill(pid, signal.SIGKILL)
+            except ProcessLookupError:
+                pass
+        raise
+
+
 @pytest.mark.parametrize("world,x_fraction", [(2, 1.0), (4, 1.0), (8, 1.0), (4, 0.45)])
 def test_nccl_ranks_match_one_gpu(world, x_fraction, cuda_device, tmp_path):
     """world ranks on world GPUs equal one GPU: energy 1e-5, forces and virial 1e-4, and
@@ -109,8 +132,7 @@ def test_nccl_ranks_match_one_gpu(world, x_fraction, cuda_device, tmp_path):
     ref_key = dst * n + src
     order = torch.argsort(ref_key)
     ref_key, ref_vec = ref_key[order].cpu(), (pos[dst] - pos[src] + shift)[order].cpu()
-    mp.start_processes(_nccl_worker, args=(world, _free_port(), str(tmp_path), n_atoms, x_fraction), nprocs=world,
-                       join=True, start_method="spawn")
+    _run_ranks(_nccl_worker, (world, _free_port(), str(tmp_path), n_atoms, x_fraction), world)
     forces = torch.full((n, 3), float("nan"))
     seen = torch.zeros(n, dtype=torch.long)
     keys, vecs, empty = [], [], 0
