@@ -65,19 +65,66 @@ def _blocks_to_e3nn_linear(weights, channels: int) -> torch.Tensor:
     return torch.cat([(w.t() * math.sqrt(channels)).reshape(-1) for w in weights])
 
 
+def _bridge_weights(module, tensors: Dict[str, torch.Tensor], where: str) -> Dict[str, torch.Tensor]:
+    """Weights of one bridge-U contraction expressed in this model's pure-U paths.
+
+    Both parameterisations are complete sets of chained couplings of the same
+    degrees, so every bridge-U coupling tensor (the checkpoint's own ``U_matrix_nu``
+    buffers, already in the ICTC basis) is an exact combination of the pure-U ones:
+    U_bridge = U_pure A.  The contraction sum_p U[..., p] W[s, p, c] is then
+    preserved by W_pure = A W_bridge.  A combination that does not reproduce the
+    checkpoint's couplings (relative residual above 1e-5) raises."""
+    import numpy as np
+    out: Dict[str, torch.Tensor] = {}
+    corr = module.correlation
+    for nu in range(1, corr + 1):
+        name = "weights_max" if nu == corr else f"weights.{corr - 1 - nu}"
+        if f"U_matrix_{nu}" not in tensors or name not in tensors:
+            raise KeyError(f"{where}: bridge-U checkpoint lacks U_matrix_{nu} or {name}")
+        u_bridge = tensors[f"U_matrix_{nu}"].detach().double().cpu().numpy()
+        u_pure = module._u64[nu]
+        if u_bridge.shape[:-1] != u_pure.shape[:-1]:
+            raise ValueError(f"{where}: U_matrix_{nu} shape {u_bridge.shape} does not match {u_pure.shape}")
+        a = u_pure.reshape(-1, u_pure.shape[-1])
+        b = u_bridge.reshape(-1, u_bridge.shape[-1])
+        coef = np.linalg.lstsq(a, b, rcond=None)[0]                      # [P_pure, P_bridge]
+        residual = np.linalg.norm(a @ coef - b) / max(np.linalg.norm(b), 1e-300)
+        if residual > 1e-5:
+            raise ValueError(f"{where}: bridge-U couplings of order {nu} are not spanned by this model's "
+                             f"(relative residual {residual:.1e})")
+        w = tensors[name]
+        mapped = torch.einsum("pq,sqc->spc", torch.from_numpy(coef).to(w.dtype), w)
+        out["weights_max" if nu == corr else f"weights.{corr - 1 - nu}"] = mapped
+    return out
+
+
 def from_reference_state_dict(model, state: Dict[str, torch.Tensor], strict: bool = True) -> List[str]:
     """Load a reference checkpoint's state dict into ``model`` (a ``MACEICTC``).
 
-    Returns the reference keys accepted as identities.  With ``strict``, unknown
-    keys and missing parameters raise."""
+    Pure-U product blocks load by name; bridge-U product blocks (the reference's
+    default, ``ICTDBridgeUSymmetricContractionSO3``) load through ``_bridge_weights``.
+    Returns the reference keys accepted as identities or as constants this model
+    does not need.  With ``strict``, unknown keys and missing parameters raise."""
     own = dict(model.named_parameters())
     own.update(dict(model.named_buffers()))
     target: Dict[str, torch.Tensor] = {}
     accepted: List[str] = []
     unknown: List[str] = []
     element_blocks: Dict[str, Dict[int, torch.Tensor]] = {}
+    bridge: Dict[tuple, Dict[str, torch.Tensor]] = {}
     for key, value in state.items():
         if value is None:
+            continue
+        m = re.fullmatch(r"products\.(\d+)\.symmetric_contractions\.symmetric_contractions\.contractions\.(\d+)\.(.+)",
+                         key)
+        if m:
+            if m[3].endswith("_zeroed"):                 # flags of all-zero U orders
+                accepted.append(key)
+            else:
+                bridge.setdefault((int(m[1]), int(m[2])), {})[m[3]] = value
+            continue
+        if re.fullmatch(r"products\.(\d+)\.symmetric_contractions\.basis_bridge\.q_\d+", key):
+            accepted.append(key)                         # already folded into the U buffers
             continue
         m = re.fullmatch(r"interactions\.(\d+)\.linear_up\.adapters\.(\d+)\.weight", key)
         if m:
@@ -117,6 +164,11 @@ def from_reference_state_dict(model, state: Dict[str, torch.Tensor], strict: boo
         unknown.append(key)
     for name, blocks in element_blocks.items():
         target[name] = torch.stack([blocks[l] for l in sorted(blocks)], 1)
+    for (i, t), tensors in bridge.items():
+        module = model.products[i].symmetric_contractions.contractions[t]
+        where = f"products.{i}.symmetric_contractions.symmetric_contractions.contractions.{t}"
+        for name, value in _bridge_weights(module, tensors, where).items():
+            target[f"products.{i}.symmetric_contractions.contractions.{t}.{name}"] = value
     if strict and unknown:
         raise NotImplementedError(f"reference keys without a counterpart in this model: {unknown}")
     with torch.no_grad():
@@ -137,6 +189,10 @@ def from_reference_state_dict(model, state: Dict[str, torch.Tensor], strict: boo
 
 # Architecture metadata a reference checkpoint must carry (the keys the reference's
 # multi-device engine requires, ``mace_ictc/interfaces/ascend_lammps.py:50-53``).
+# Product backends whose checkpoints load onto this model: pure-U by name, bridge-U
+# through the exact change of coupling basis (``_bridge_weights``).
+PRODUCT_BACKENDS = ("ictd-pure-u", "ictd-bridge-u")
+
 REQUIRED_METADATA = ("channel_in", "lmax", "num_interaction", "avg_num_neighbors", "radial_sqrt_num_basis",
                      "polynomial_cutoff_p", "ictd_fix_product_backend")
 
@@ -166,7 +222,9 @@ def check_reference_metadata(model, metadata: Dict[str, object]):
         if key not in want:
             continue
         mine = want[key]
-        if isinstance(mine, float) or isinstance(value, float):
+        if key == "ictd_fix_product_backend":
+            same = str(value) in PRODUCT_BACKENDS
+        elif isinstance(mine, float) or isinstance(value, float):
             same = abs(float(value) - float(mine)) <= 1e-9 * max(1.0, abs(float(mine)))
         elif isinstance(mine, bool):
             same = bool(value) == mine

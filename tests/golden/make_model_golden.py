@@ -27,6 +27,18 @@ script registers stand-in modules before importing it:
 * every other e3nn entry point the import touches raises when called.
 So the fixtures pin everything on this path against the reference code itself,
 and the product block's linear against the stated o3.Linear semantics.
+
+The bridge-U case (``ictd-bridge-u``, the reference's default product backend) also
+runs the reference's e3nn-basis construction: its MACE coupling recursion
+(``ictc_o3/basis/_mace_cg.py:41-175``), the basis-bridge fit and the fold of the
+bridge into the U tensors (``ictc_o3/ops/symmetric_contraction.py:24-180``).  For
+it, ``o3.spherical_harmonics`` and ``o3.wigner_3j`` are stand-ins expressed in a
+seeded random orthonormal basis per degree (the ICTC harmonics rotated by it, and
+the ICTC couplings rotated the same way, unit Frobenius norm, each with a random
+sign): a real basis with its own conventions, as e3nn's is.  The bridge-U couplings
+the reference derives from them are stored with the parameters, as in its
+checkpoints; the model here must load them through an exact change of coupling
+basis whatever those conventions are.
 """
 import math
 import os
@@ -150,6 +162,30 @@ def install_import_stand_ins():
     sys.modules["opt_einsum_fx"] = einsum_fx
 
 
+def install_basis_stand_ins(seed):
+    """e3nn primitives of the bridge-U construction in a seeded random real basis."""
+    from ictc_o3.basis import ictd_irreps
+    o3 = sys.modules["e3nn.o3"]
+    gen = torch.Generator().manual_seed(seed)
+    rot = {l: torch.linalg.qr(torch.randn(2 * l + 1, 2 * l + 1, generator=gen, dtype=torch.float64))[0]
+           for l in range(8)}
+    signs = {}
+
+    def spherical_harmonics(irreps, x, normalize=True, normalization="component"):
+        irreps = o3.Irreps(irreps)
+        ys = ictd_irreps.direction_harmonics_all(x / x.norm(dim=-1, keepdim=True), irreps.lmax)
+        return torch.cat([ys[mul_ir.ir.l].to(torch.float64) @ rot[mul_ir.ir.l] for mul_ir in irreps], -1)
+
+    def wigner_3j(l1, l2, l3, dtype=None, **_):
+        c = torch.as_tensor(ictd_irreps.build_full_cg_tensor_so3(l2, l3, l1)).permute(2, 0, 1)
+        c = torch.einsum("oab,oi,aj,bk->ijk", c, rot[l1], rot[l2], rot[l3])
+        if (l1, l2, l3) not in signs:
+            signs[(l1, l2, l3)] = 1.0 if torch.rand(1, generator=gen).item() < 0.5 else -1.0
+        return (signs[(l1, l2, l3)] * c / c.norm()).to(dtype or torch.get_default_dtype())
+
+    o3.spherical_harmonics, o3.wigner_3j = spherical_harmonics, wigner_3j
+
+
 def periodic_system(n, side, cutoff, seed):
     """Random atoms in a cube with a minimum distance of 0.9 A and the minimum-image
     edges within the cutoff: r_e = pos[dst] - pos[src] + shift_e."""
@@ -169,7 +205,7 @@ def periodic_system(n, side, cutoff, seed):
     return pos, numbers, j, i, shift[i, j]
 
 
-def model_case(name, channels, lmax, n_atoms, side, cutoff, seed):
+def model_case(name, channels, lmax, n_atoms, side, cutoff, seed, product_backend="ictd-pure-u"):
     from mace_ictc.models.factory import build_baseline_model
     from mace_ictc.utils.config import ModelConfig
     torch.manual_seed(seed)
@@ -179,7 +215,7 @@ def model_case(name, channels, lmax, n_atoms, side, cutoff, seed):
                       irreps_output_conv_channels=channels, lmax=lmax, max_radius=cutoff, max_radius_main=cutoff,
                       function_type="bessel")
     model = build_baseline_model(cfg, avg_num_neighbors=avg, num_interaction=2, route="baseline",
-                                 product_backend="ictd-pure-u", correlation=3, use_reduced_cg=False,
+                                 product_backend=product_backend, correlation=3, use_reduced_cg=False,
                                  freeze_conv_tp_weight=True, radial_sqrt_num_basis=False, edge_lmax=lmax,
                                  attn_heads=0, atomic_numbers=[1, 6, 8], ictd_save_tp_mode="fully-connected",
                                  invariant_channels=32, device=torch.device("cpu"), dtype=dtype)
@@ -197,6 +233,12 @@ def model_case(name, channels, lmax, n_atoms, side, cutoff, seed):
               "shift": shift.numpy(), "atomic_energy": atomic.detach().numpy(), "forces": -grad.numpy()}
     for key, param in model.named_parameters():
         record["param:" + key] = param.detach().numpy()
+    if product_backend == "ictd-bridge-u":          # its checkpoints carry the folded couplings
+        params = dict(model.named_parameters())
+        for key, value in model.state_dict().items():
+            if key not in params and ".symmetric_contractions." in key and value is not None:
+                record["buffer:" + key] = value.detach().numpy()
+    record["product_backend"] = product_backend
     np.savez_compressed(os.path.join(HERE, name), **record)
     print(name, "energy", float(atomic.sum()), "edges", src.numel(), "params", len(list(model.parameters())))
 
@@ -210,6 +252,15 @@ def main():
     sys.path.insert(0, root)
     model_case("model_c8_l2.npz", channels=8, lmax=2, n_atoms=40, side=8.0, cutoff=3.0, seed=11)
     model_case("model_c8_l3.npz", channels=8, lmax=3, n_atoms=36, side=8.0, cutoff=3.0, seed=21)
+    o3 = sys.modules["e3nn.o3"]
+    # Irrep products, membership and counts, used by the MACE coupling recursion
+    o3.Irrep.__mul__ = lambda a, b: [o3.Irrep(l, a.p * o3.Irrep(b).p)
+                                     for l in range(abs(a.l - o3.Irrep(b).l), a.l + o3.Irrep(b).l + 1)]
+    o3.Irreps.__contains__ = lambda irreps, ir: o3.Irrep(ir) in [x.ir for x in irreps]
+    o3.Irreps.count = lambda irreps, ir: sum(x.mul for x in irreps if x.ir == o3.Irrep(ir))
+    install_basis_stand_ins(seed=7)
+    model_case("model_c8_l2_bridge.npz", channels=8, lmax=2, n_atoms=40, side=8.0, cutoff=3.0, seed=31,
+               product_backend="ictd-bridge-u")
 
 
 if __name__ == "__main__":

@@ -80,7 +80,9 @@ def test_checkpoint_metadata_is_checked():
     ckpt = {"e3trans_state_dict": to_reference_state_dict(model), "model_hyperparameters": meta,
             "dtype": "float32", "tensor_product_mode": "pure-cartesian-ictd-fix"}
     load_reference_checkpoint(model, ckpt)
-    for key, value in (("radial_sqrt_num_basis", True), ("ictd_fix_product_backend", "ictd-bridge-u"),
+    bridge = dict(ckpt, model_hyperparameters=dict(meta, ictd_fix_product_backend="ictd-bridge-u"))
+    load_reference_checkpoint(model, bridge)      # bridge-U metadata is accepted (weights map exactly)
+    for key, value in (("radial_sqrt_num_basis", True), ("ictd_fix_product_backend", "native-mace"),
                        ("ictd_fix_first_layer_self_connection", False), ("avg_num_neighbors", 7.5),
                        ("lmax", 3)):
         bad = dict(ckpt, model_hyperparameters=dict(meta, **{key: value}))

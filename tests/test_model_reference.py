@@ -1,10 +1,12 @@
 """The model against the reference's own MACE-ICTC model (CPU, FP64 oracle operators).
 
 Fixtures from ``tests/golden/make_model_golden.py``: the reference
-``PureCartesianICTDFix`` (pure-ICTC product backend, reference defaults for new
-models, random weights) evaluated by its own forward on small periodic systems.
-Its parameters load through ``mace_ictc.checkpoint.from_reference_state_dict``;
-per-atom energies and forces must match to FP64 rounding.
+``PureCartesianICTDFix`` (pure-ICTC and bridge-U product backends, reference
+defaults for new models, random weights) evaluated by its own forward on small
+periodic systems.  Its state dict loads through
+``mace_ictc.checkpoint.from_reference_state_dict`` (bridge-U weights through the
+exact change of coupling basis); per-atom energies and forces must match to FP64
+rounding.
 """
 import numpy as np
 import pytest
@@ -12,7 +14,8 @@ import torch
 
 from conftest import golden
 
-CASES = ["model_c8_l2.npz", "model_c8_l3.npz"]
+# pure-U at lmax 2 and 3; bridge-U (the reference's default product backend) at lmax 2
+CASES = ["model_c8_l2.npz", "model_c8_l3.npz", "model_c8_l2_bridge.npz"]
 
 
 def load_case(name, ops=None, dtype=torch.float64, device="cpu"):
@@ -20,7 +23,8 @@ def load_case(name, ops=None, dtype=torch.float64, device="cpu"):
     from mace_ictc.checkpoint import from_reference_state_dict
     from mace_ictc.models import MACEICTC
     rec = golden(name)
-    state = {k[len("param:"):]: torch.from_numpy(v) for k, v in rec.items() if k.startswith("param:")}
+    state = {k.split(":", 1)[1]: torch.from_numpy(v) for k, v in rec.items()
+             if k.startswith("param:") or k.startswith("buffer:")}
     model = MACEICTC(channels=int(rec["channels"]), lmax=int(rec["lmax"]), num_interactions=2, correlation=3,
                      r_max=float(rec["cutoff"]), avg_num_neighbors=float(rec["avg_num_neighbors"]), ops=ops)
     model = model.to(dtype)
