@@ -79,6 +79,66 @@ def _table_rows(lmax: int, correlation: int, target_lmax: int) -> int:
 
 
 # ---------------------------------------------------------------------------
+# The contraction module as the kernels see it
+# ---------------------------------------------------------------------------
+
+def contraction_blocks(owner):
+    """Per-target blocks in target order: ``owner.contractions`` (this package's
+    modules) or ``owner.symmetric_contractions.contractions`` (the reference's
+    bridge-U module, ``ictc_o3/ops/symmetric_contraction.py:116-122``, whose blocks
+    are MACE contractions holding ``U_matrix_nu`` buffers, ``weights_max`` and
+    ``weights``)."""
+    try:
+        blocks = owner.contractions
+    except AttributeError:
+        blocks = owner.symmetric_contractions.contractions
+    return list(blocks)
+
+
+def block_weights(block) -> torch.Tensor:
+    """[S, sum P, C], weight columns ordered nu = corr, corr-1, ..., 1."""
+    return torch.cat([block.weights_max, *block.weights], 1)
+
+
+def block_table(block, device, dtype=torch.float32) -> torch.Tensor:
+    """Symmetrised couplings of one block, [rows * (2t+1), sum P].
+
+    This package's blocks build and cache their own.  A reference block's are
+    built from its ``U_matrix_nu`` buffers (output degree from the shape of
+    ``U_matrix_1``: [D, P] for degree 0, [2t+1, D, P] otherwise) and kept on the
+    block while the buffers are unchanged."""
+    own = getattr(block, "symmetric_table", None)
+    if own is not None:
+        return own(device, dtype)
+    corr = int(block.correlation)
+    buffers = [block.U_tensors(nu) for nu in range(1, corr + 1)]
+    version = tuple((u.data_ptr(), u._version, tuple(u.shape)) for u in buffers)
+    cache = block.__dict__.setdefault("_cuda_symmetric_tables", {})
+    key = (str(device), dtype)
+    hit = cache.get(key)
+    if hit is not None and hit[0] == version:
+        return hit[1]
+    u64 = {nu: u.detach().double().cpu().numpy() for nu, u in zip(range(1, corr + 1), buffers)}
+    output_l = 0 if u64[1].ndim == 2 else (u64[1].shape[0] - 1) // 2
+    sym = symmetric_table(u64, output_l, u64[1].shape[-2], corr)
+    table = torch.from_numpy(sym.reshape(-1, sym.shape[-1])).to(device=device, dtype=dtype)
+    cache[key] = (version, table)
+    return table
+
+
+def contraction_spec(owner):
+    """(channels, lmax, correlation, target_lmax, num_elements) of a contraction module;
+    correlation and element count are read from its blocks, which every variant has."""
+    blocks = contraction_blocks(owner)
+    orders = {int(b.correlation) for b in blocks}
+    target = int(owner.target_lmax)
+    if len(orders) != 1 or len(blocks) != target + 1:
+        raise ValueError("The CUDA symmetric contraction needs one block per target degree, all of one "
+                         "correlation order")
+    return int(owner.channels), int(owner.lmax), orders.pop(), target, int(blocks[0].weights_max.shape[0])
+
+
+# ---------------------------------------------------------------------------
 # Species tiles
 # ---------------------------------------------------------------------------
 
@@ -362,21 +422,22 @@ def coefficient_table(owner, device):
 
     Differentiable in the weights.  When no weight needs a gradient (frozen weights,
     or gradients disabled), the folded table is kept and reused until a weight
-    changes (same tensors and versions)."""
-    weights = [c.stacked_weights() for c in owner.contractions]                 # [S, P_t, C] each
-    usyms = tuple(c.symmetric_table(device, torch.float32) for c in owner.contractions)
+    changes (same tensors and versions) or a block's coupling table is rebuilt."""
+    blocks = contraction_blocks(owner)
+    weights = [block_weights(c) for c in blocks]                                # [S, P_t, C] each
+    usyms = tuple(block_table(c, device, torch.float32) for c in blocks)
     rows = tuple(int(u.shape[0]) for u in usyms)
-    params = [p for c in owner.contractions for p in c.parameters()]
+    params = [p for c in blocks for p in c.parameters()]
     live = torch.is_grad_enabled() and any(p.requires_grad for p in params)
     if live:
         return _Fold.apply(usyms, rows, *weights)
     key = (str(device), tuple((p.data_ptr(), p._version) for p in params))
     cached = owner.__dict__.get("_cuda_folded_table")
-    if cached is not None and cached[0] == key:
+    if cached is not None and cached[0] == key and all(a is b for a, b in zip(cached[2], usyms)):
         return cached[1]
     with torch.no_grad():
         table = _Fold.apply(usyms, rows, *[w.detach() for w in weights])
-    owner.__dict__["_cuda_folded_table"] = (key, table)
+    owner.__dict__["_cuda_folded_table"] = (key, table, usyms)
     return table
 
 
@@ -384,17 +445,20 @@ def contract_flat(owner, node_feats: torch.Tensor, index: torch.Tensor) -> torch
     """node_feats [N, C(L+1)^2] mul_ir flat -> [N, C(Lt+1)^2] mul_ir flat."""
     if node_feats.dtype != torch.float32 or node_feats.device.type != "cuda":
         raise ValueError("The CUDA symmetric contraction requires CUDA FP32 node features")
-    channels, lmax, corr, target = owner.channels, owner.lmax, owner.correlation, owner.target_lmax
+    channels, lmax, corr, target, num_elements = contraction_spec(owner)
     table = coefficient_table(owner, node_feats.device)
     if table.shape[1] != _table_rows(lmax, corr, target):
         raise ValueError("coefficient table does not match the kernel row count")
-    tiles, tile_species = species_tiles(index.to(node_feats.device), owner.num_elements)
-    spec = (int(channels), int(lmax), int(corr), int(target))
+    tiles, tile_species = species_tiles(index.to(node_feats.device), num_elements)
+    spec = (channels, lmax, corr, target)
     return _Contraction.apply(spec, tiles, tile_species, node_feats.contiguous(), table)
 
 
 def factorized_contractions(owner, x: torch.Tensor, index: torch.Tensor) -> torch.Tensor:
-    """Reference signature (``backends/ascend/contraction.py:8``): x [N, C, sum(2l+1)] -> [N, C(Lt+1)^2]."""
+    """Reference signature (``backends/ascend/contraction.py:8``): x [N, C, sum(2l+1)] -> [N, C(Lt+1)^2].
+
+    ``owner`` is a contraction module of this package or the reference's own
+    bridge-U module (the object at its hook site, ``ictc_o3/ops/symmetric_contraction.py:189-193``)."""
     n, channels = x.shape[0], owner.channels
     flat = torch.cat([x[:, :, l * l:(l + 1) ** 2].reshape(n, channels * (2 * l + 1))
                       for l in range(owner.lmax + 1)], -1)

@@ -173,10 +173,14 @@ def direction_harmonics(directions, lmax, *, policy="auto"):
 
 
 def configure_symmetric_contraction(module, *, policy="auto", training=False):
-    """Select the CUDA contraction for a module (reference ``operators.py:189-201``)."""
-    from ictc_o3.ops.symmetric_contraction import ICTDPureUSymmetricContractionSO3
-    if not isinstance(module, ICTDPureUSymmetricContractionSO3):
-        raise TypeError("Expected an ICTC symmetric contraction")
+    """Select the CUDA contraction for a module (reference ``operators.py:189-201``).
+
+    Accepts the bridge-U module the reference requires and the pure-ICTC one; both
+    run on the same kernels."""
+    from ictc_o3.ops.symmetric_contraction import (ICTDBridgeUSymmetricContractionSO3,
+                                                   ICTDPureUSymmetricContractionSO3)
+    if not isinstance(module, (ICTDBridgeUSymmetricContractionSO3, ICTDPureUSymmetricContractionSO3)):
+        raise TypeError("Expected an ICTC bridge-U (or pure-ICTC) symmetric contraction")
     if policy not in ("auto", "generated", "reference"):
         raise ValueError("policy must be auto, generated or reference")
     require_cuda_fp32(*module.parameters())
@@ -189,7 +193,9 @@ def configure_symmetric_contraction(module, *, policy="auto", training=False):
 
 def create_symmetric_contraction(*, num_elements, lmax, target_lmax=None, channels=64,
                                  correlation=3, device="cuda", policy="generated", training=False):
-    """Reference ``operators.py:204-218``, CUDA device."""
+    """Reference ``operators.py:204-218``, CUDA device: a bridge-U module (the
+    reference's class), whose couplings are the ICTC ones until a reference state
+    dict is loaded into it."""
     for value, name in ((num_elements, "num_elements"), (channels, "channels"), (correlation, "correlation")):
         _positive_integer(value, name)
     if correlation not in (1, 2, 3):
@@ -199,9 +205,9 @@ def create_symmetric_contraction(*, num_elements, lmax, target_lmax=None, channe
     _degree(target_lmax, "target_lmax")
     if torch.device(device).type != "cuda":
         raise ValueError("This operator factory requires a CUDA device")
-    from ictc_o3.ops.symmetric_contraction import ICTDPureUSymmetricContractionSO3
-    module = ICTDPureUSymmetricContractionSO3(num_elements=num_elements, channels=channels, lmax=lmax,
-                                              target_lmax=target_lmax, correlation=correlation)
+    from ictc_o3.ops.symmetric_contraction import ICTDBridgeUSymmetricContractionSO3
+    module = ICTDBridgeUSymmetricContractionSO3(num_elements=num_elements, channels=channels, lmax=lmax,
+                                                target_lmax=target_lmax, correlation=correlation)
     module = module.to(device=device, dtype=torch.float32)
     configure_symmetric_contraction(module, policy=policy, training=training)
     return module

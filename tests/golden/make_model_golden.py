@@ -39,6 +39,11 @@ sign): a real basis with its own conventions, as e3nn's is.  The bridge-U coupli
 the reference derives from them are stored with the parameters, as in its
 checkpoints; the model here must load them through an exact change of coupling
 basis whatever those conventions are.
+
+Two contraction cases (``sc_bridge_*.npz``) hold the reference's bridge-U module on
+its own, built the same way: its complete state dict (folded couplings, basis
+bridge, weights, zero flags), random flat ICTC features with species, and its
+outputs through the element-selected and the one-hot forward routes.
 """
 import math
 import os
@@ -243,6 +248,38 @@ def model_case(name, channels, lmax, n_atoms, side, cutoff, seed, product_backen
     print(name, "energy", float(atomic.sum()), "edges", src.numel(), "params", len(list(model.parameters())))
 
 
+def contraction_case(name, channels, lmax, target_lmax, nodes, seed):
+    """The reference's bridge-U module alone (``ICTDBridgeUSymmetricContractionSO3``,
+    ``ictc_o3/ops/symmetric_contraction.py:92-206``): its whole state dict, random
+    flat ICTC features and species, and its outputs through both forward routes
+    (element-selected weights and one-hot attributes)."""
+    from ictc_o3.ops.symmetric_contraction import ICTDBridgeUSymmetricContractionSO3
+    torch.manual_seed(seed)
+    dtype = torch.float64
+    torch.set_default_dtype(dtype)
+    try:
+        module = ICTDBridgeUSymmetricContractionSO3(num_elements=3, channels=channels, lmax=lmax,
+                                                    target_lmax=target_lmax, correlation=3)
+    finally:
+        torch.set_default_dtype(torch.float32)
+    module = module.to(dtype)
+    with torch.no_grad():
+        for param in module.parameters():
+            param.copy_(torch.randn(param.shape, dtype=dtype) / math.sqrt(param.shape[-2]))
+    x = 0.7 * torch.randn(nodes, channels * (lmax + 1) ** 2, dtype=dtype)
+    species = torch.randint(0, 3, (nodes,))
+    attrs = torch.nn.functional.one_hot(species, 3).to(dtype)
+    with torch.no_grad():
+        selected = module(x, attrs, species)
+        one_hot = module(x, attrs)
+    record = {"channels": channels, "lmax": lmax, "target_lmax": target_lmax, "x": x.numpy(),
+              "species": species.numpy(), "out": selected.numpy(), "out_one_hot": one_hot.numpy()}
+    for key, value in module.state_dict().items():
+        record["state:" + key] = value.detach().numpy()
+    np.savez_compressed(os.path.join(HERE, name), **record)
+    print(name, "out norm", float(selected.norm()), "state keys", len(module.state_dict()))
+
+
 def main():
     root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("ICTC_REFERENCE_ROOT")
     if not root:
@@ -261,6 +298,8 @@ def main():
     install_basis_stand_ins(seed=7)
     model_case("model_c8_l2_bridge.npz", channels=8, lmax=2, n_atoms=40, side=8.0, cutoff=3.0, seed=31,
                product_backend="ictd-bridge-u")
+    contraction_case("sc_bridge_c8_l2_t2.npz", channels=8, lmax=2, target_lmax=2, nodes=37, seed=41)
+    contraction_case("sc_bridge_c4_l3_t1.npz", channels=4, lmax=3, target_lmax=1, nodes=29, seed=43)
 
 
 if __name__ == "__main__":

@@ -43,6 +43,45 @@ def test_contraction_matches_reference(name, cuda_device):
             k += 1
 
 
+@pytest.mark.parametrize("name", ["sc_bridge_c8_l2_t2.npz", "sc_bridge_c4_l3_t1.npz"])
+def test_bridge_module_matches_reference_module(name, cuda_device):
+    """A state dict of the reference's bridge-U module, loaded into the module of the
+    same name, through the CUDA kernels (FP32) against the reference module's FP64
+    outputs; the feature gradient against the FP64 recursion over the same couplings."""
+    from ictc_o3.operators import configure_symmetric_contraction
+    from test_contraction_bridge import _module, _oracle
+    g = golden(name)
+    module = _module(g).float().to(cuda_device)
+    assert configure_symmetric_contraction(module)["backend"] == "cuda"
+    x = torch.from_numpy(g["x"]).float().to(cuda_device).requires_grad_(True)
+    species = torch.from_numpy(g["species"]).to(cuda_device)
+    attrs = torch.nn.functional.one_hot(species, 3).float()
+    out = module(x, attrs, species)
+    assert_close(out.detach().cpu(), torch.from_numpy(g["out"]), 1e-5, 1e-3, "bridge-U forward")
+    assert_close(module(x, attrs).detach().cpu(), torch.from_numpy(g["out_one_hot"]), 1e-5, 1e-3,
+                 "bridge-U forward (one-hot attributes)")
+    G = torch.randn(out.shape, device=cuda_device, generator=torch.Generator(device=cuda_device).manual_seed(5))
+    (dx,) = torch.autograd.grad(out, [x], G)
+    x64 = torch.from_numpy(g["x"]).requires_grad_(True)
+    ref = _oracle(_module(g), x64, torch.from_numpy(g["species"]))
+    (rdx,) = torch.autograd.grad(ref, [x64], G.double().cpu())
+    assert_close(dx.cpu(), rdx, 1e-4, 1e-3, "bridge-U dx")
+
+
+@pytest.mark.parametrize("name", ["sc_bridge_c8_l2_t2.npz", "sc_bridge_c4_l3_t1.npz"])
+def test_hook_entry_with_reference_layout_owner(name, cuda_device):
+    """``factorized_contractions`` given an object laid out like the reference's own
+    bridge-U module (what its hook site passes) and MACE-layout features."""
+    from ictc_o3.backends.cuda.contraction import factorized_contractions
+    from oracle.sc_oracle import flat_to_mace
+    from test_contraction_bridge import reference_layout_module
+    g = golden(name)
+    owner = reference_layout_module(g).float().to(cuda_device)
+    x = flat_to_mace(torch.from_numpy(g["x"]).float(), int(g["channels"]), int(g["lmax"])).to(cuda_device)
+    out = factorized_contractions(owner, x.contiguous(), torch.from_numpy(g["species"]).to(cuda_device))
+    assert_close(out.detach().cpu(), torch.from_numpy(g["out"]), 1e-5, 1e-3, "hook entry, reference-layout owner")
+
+
 @pytest.mark.parametrize("lmax,target,corr", [(1, 1, 3), (2, 2, 3), (2, 0, 3), (3, 3, 3), (2, 2, 2), (3, 1, 1)])
 @pytest.mark.parametrize("channels", [32, 96, 40])
 def test_contraction_random_against_oracle(lmax, target, corr, channels, cuda_device):
