@@ -3,7 +3,7 @@
 Maps the parameter names of the reference model
 (``mace_ictc/models/pure_cartesian_ictd_fix.py:2058-2765``) onto ``MACEICTC`` for
 the configuration this backend implements (residual interaction blocks with the
-path-preserving TP, pure-ICTC symmetric contraction product blocks, linear layer
+path-preserving TP, pure-ICTC or bridge-U symmetric contraction product blocks, linear layer
 readouts and the MLP last readout):
 
 ==============================================================  =====================================
@@ -17,6 +17,8 @@ interactions.i.message_linear.weights.l         (:629-661)      interactions.i.m
 interactions.i.self_connection.weights.l        (:335-392)      interactions.i.self_connection.weight[:, l]
 interactions.i.message_selector.weights.l                       interactions.i.message_selector.weight[:, l]
 products.i.symmetric_contractions.contractions.t.*  (:1202-1395) same names (weights_max, weights.j, U_matrix_nu)
+products.i.symmetric_contractions.symmetric_contractions.*      bridge-U model: same names; pure-U model:
+  (bridge-U, ops/symmetric_contraction.py:92-206)               weights mapped by ``_bridge_weights``
 products.i.linear.weight  (e3nn o3.Linear, :1419)               products.i.linear.weights.l
 layer_energy_readouts.i.readout.weight                          layer_readouts.i.weight
 last_layer_energy_readout.linear_{1,2}.weight   (:1434-1449)    last_readout.{0,2}.weight
@@ -98,13 +100,29 @@ def _bridge_weights(module, tensors: Dict[str, torch.Tensor], where: str) -> Dic
     return out
 
 
+def _load_bridge_module(module, sub: Dict[str, torch.Tensor], prefix: str, strict: bool, unknown: List[str]):
+    """Load reference product-block tensors (bridge-U names, or pure-U names moved
+    under ``symmetric_contractions.``) into a bridge-U product module of this model:
+    couplings, weights, zero flags and bridge matrices by name, coupling counts
+    resized to the checkpoint's."""
+    result = module.load_state_dict(sub, strict=False)
+    unknown.extend(prefix + k for k in result.unexpected_keys)
+    if strict:
+        missing = [prefix + n for n, _ in module.named_parameters() if n not in sub]
+        if missing:
+            raise KeyError(f"parameters not set by the reference checkpoint: {missing}")
+
+
 def from_reference_state_dict(model, state: Dict[str, torch.Tensor], strict: bool = True) -> List[str]:
     """Load a reference checkpoint's state dict into ``model`` (a ``MACEICTC``).
 
-    Pure-U product blocks load by name; bridge-U product blocks (the reference's
-    default, ``ICTDBridgeUSymmetricContractionSO3``) load through ``_bridge_weights``.
-    Returns the reference keys accepted as identities or as constants this model
-    does not need.  With ``strict``, unknown keys and missing parameters raise."""
+    Product blocks: into a pure-U model, pure-U checkpoints load by name and bridge-U
+    ones (the reference's default, ``ICTDBridgeUSymmetricContractionSO3``) through
+    ``_bridge_weights``; into a bridge-U model (``product_backend="ictd-bridge-u"``)
+    both load by name, the couplings with them.  Returns the reference keys accepted
+    as identities or as constants this model does not need.  With ``strict``,
+    unknown keys and missing parameters raise."""
+    from ictc_o3.ops.symmetric_contraction import ICTDBridgeUSymmetricContractionSO3
     own = dict(model.named_parameters())
     own.update(dict(model.named_buffers()))
     target: Dict[str, torch.Tensor] = {}
@@ -112,19 +130,33 @@ def from_reference_state_dict(model, state: Dict[str, torch.Tensor], strict: boo
     unknown: List[str] = []
     element_blocks: Dict[str, Dict[int, torch.Tensor]] = {}
     bridge: Dict[tuple, Dict[str, torch.Tensor]] = {}
+    direct: Dict[int, Dict[str, torch.Tensor]] = {}     # product blocks of a bridge-U model, by name
+    loaded: set = set()
+
+    def bridge_model(i: int) -> bool:
+        return i < len(model.products) and isinstance(model.products[i].symmetric_contractions,
+                                                      ICTDBridgeUSymmetricContractionSO3)
+
     for key, value in state.items():
         if value is None:
             continue
-        m = re.fullmatch(r"products\.(\d+)\.symmetric_contractions\.symmetric_contractions\.contractions\.(\d+)\.(.+)",
-                         key)
+        m = re.fullmatch(r"products\.(\d+)\.symmetric_contractions\."
+                         r"(symmetric_contractions\.contractions\.(\d+)\.(.+)|basis_bridge\.q_\d+)", key)
+        if m and bridge_model(int(m[1])):
+            direct.setdefault(int(m[1]), {})[m[2]] = value
+            continue
+        if m and m[3] is None:
+            accepted.append(key)                         # already folded into the U buffers
+            continue
         if m:
-            if m[3].endswith("_zeroed"):                 # flags of all-zero U orders
+            if m[4].endswith("_zeroed"):                 # flags of all-zero U orders
                 accepted.append(key)
             else:
-                bridge.setdefault((int(m[1]), int(m[2])), {})[m[3]] = value
+                bridge.setdefault((int(m[1]), int(m[3])), {})[m[4]] = value
             continue
-        if re.fullmatch(r"products\.(\d+)\.symmetric_contractions\.basis_bridge\.q_\d+", key):
-            accepted.append(key)                         # already folded into the U buffers
+        m = re.fullmatch(r"products\.(\d+)\.symmetric_contractions\.(contractions\.\d+\..+)", key)
+        if m and bridge_model(int(m[1])):
+            direct.setdefault(int(m[1]), {})["symmetric_contractions." + m[2]] = value
             continue
         m = re.fullmatch(r"interactions\.(\d+)\.linear_up\.adapters\.(\d+)\.weight", key)
         if m:
@@ -169,6 +201,10 @@ def from_reference_state_dict(model, state: Dict[str, torch.Tensor], strict: boo
         where = f"products.{i}.symmetric_contractions.symmetric_contractions.contractions.{t}"
         for name, value in _bridge_weights(module, tensors, where).items():
             target[f"products.{i}.symmetric_contractions.contractions.{t}.{name}"] = value
+    for i, sub in direct.items():
+        prefix = f"products.{i}.symmetric_contractions."
+        _load_bridge_module(model.products[i].symmetric_contractions, sub, prefix, strict, unknown)
+        loaded.update(prefix + n for n, _ in model.products[i].symmetric_contractions.named_parameters())
     if strict and unknown:
         raise NotImplementedError(f"reference keys without a counterpart in this model: {unknown}")
     with torch.no_grad():
@@ -181,7 +217,7 @@ def from_reference_state_dict(model, state: Dict[str, torch.Tensor], strict: boo
                 raise ValueError(f"{name}: shape {tuple(value.shape)} does not match {tuple(own[name].shape)}")
             own[name].copy_(value)
     if strict:
-        missing = [n for n, p in model.named_parameters() if n not in target]
+        missing = [n for n, p in model.named_parameters() if n not in target and n not in loaded]
         if missing:
             raise KeyError(f"parameters not set by the reference checkpoint: {missing}")
     return accepted
@@ -189,8 +225,9 @@ def from_reference_state_dict(model, state: Dict[str, torch.Tensor], strict: boo
 
 # Architecture metadata a reference checkpoint must carry (the keys the reference's
 # multi-device engine requires, ``mace_ictc/interfaces/ascend_lammps.py:50-53``).
-# Product backends whose checkpoints load onto this model: pure-U by name, bridge-U
-# through the exact change of coupling basis (``_bridge_weights``).
+# Product backends whose checkpoints load onto this model (either backend): by name,
+# or through the exact change of coupling basis (``_bridge_weights``) when a bridge-U
+# checkpoint meets pure-U product blocks.
 PRODUCT_BACKENDS = ("ictd-pure-u", "ictd-bridge-u")
 
 REQUIRED_METADATA = ("channel_in", "lmax", "num_interaction", "avg_num_neighbors", "radial_sqrt_num_basis",
@@ -201,7 +238,7 @@ def model_metadata(model) -> Dict[str, object]:
     """The reference metadata values that describe ``model``."""
     return {"channel_in": model.channels, "lmax": model.lmax, "num_interaction": len(model.interactions),
             "avg_num_neighbors": model.avg_num_neighbors, "radial_sqrt_num_basis": model.radial_sqrt_num_basis,
-            "polynomial_cutoff_p": model.p, "ictd_fix_product_backend": "ictd-pure-u",
+            "polynomial_cutoff_p": model.p, "ictd_fix_product_backend": model.product_backend,
             "ictd_fix_first_layer_self_connection": model.first_layer_self_connection,
             "max_radius": model.r_max, "tensor_product_mode": "pure-cartesian-ictd-fix", "dtype": "float32"}
 

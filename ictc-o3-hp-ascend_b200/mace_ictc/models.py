@@ -33,7 +33,8 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from ictc_o3.basis.ictd_irreps import EdgeWeightedPathPreservingTensorProduct, operator_paths
-from ictc_o3.ops.symmetric_contraction import ICTDPureUSymmetricContractionSO3
+from ictc_o3.ops.symmetric_contraction import (ICTDBridgeUSymmetricContractionSO3,
+                                               ICTDPureUSymmetricContractionSO3)
 
 SILU_SCALE = 1.6791767923989418  # normalised SiLU (pure_cartesian_ictd_fix.py:610-619)
 
@@ -245,11 +246,15 @@ class InteractionBlock(nn.Module):
         return message, self.self_connection(sc_in, groups, species)
 
 
+PRODUCT_MODULES = {"ictd-pure-u": ICTDPureUSymmetricContractionSO3,
+                   "ictd-bridge-u": ICTDBridgeUSymmetricContractionSO3}
+
+
 class ProductBlock(nn.Module):
-    def __init__(self, *, channels, lmax, target_lmax, correlation, num_elements):
+    def __init__(self, *, channels, lmax, target_lmax, correlation, num_elements, product_backend="ictd-pure-u"):
         super().__init__()
         self.channels, self.target_lmax = channels, target_lmax
-        self.symmetric_contractions = ICTDPureUSymmetricContractionSO3(
+        self.symmetric_contractions = PRODUCT_MODULES[product_backend](
             num_elements=num_elements, channels=channels, lmax=lmax, target_lmax=target_lmax,
             correlation=correlation)
         self.linear = ChannelLinearSO3(channels, channels, target_lmax)
@@ -269,14 +274,26 @@ class MACEICTC(nn.Module):
 
     def __init__(self, *, num_elements=None, channels=64, lmax=2, num_interactions=2, correlation=3, r_max=5.0,
                  num_basis=8, polynomial_cutoff_p=5, avg_num_neighbors=1.0, readout_hidden=16, ops=None,
-                 atomic_numbers=(1, 6, 8), first_layer_self_connection=True, radial_sqrt_num_basis=False):
+                 atomic_numbers=(1, 6, 8), first_layer_self_connection=True, radial_sqrt_num_basis=False,
+                 product_backend="ictd-pure-u"):
         """Defaults follow the reference constructor for new models: atomic numbers
         H, C, O (``mace_ictc/hp/runtime.py:7``), an element-conditioned scalar
         self-connection in the first layer (``mace_ictc/models/factory.py:17``,
         ``pure_cartesian_ictd_fix.py:2393-2395``) and the radial embedding without
         the sqrt(num_basis) factor (``radial_sqrt_num_basis=False``, :2191, :2325).
-        ``num_elements`` (if given) must equal ``len(atomic_numbers)``."""
+        A ``num_elements`` that differs from ``len(atomic_numbers)`` makes the
+        elements anonymous: atomic numbers 1..num_elements.
+
+        ``product_backend`` picks the symmetric-contraction parameterisation of the
+        product blocks, with the reference's names (``ictd_fix_product_backend``,
+        :2166): "ictd-pure-u" (ICTC couplings) or "ictd-bridge-u" (the reference's
+        default; the couplings are buffers that its checkpoints overwrite).  Both run
+        the same kernels and span the same couplings; checkpoints of either load
+        into a model of either."""
         super().__init__()
+        if product_backend not in PRODUCT_MODULES:
+            raise ValueError(f"product_backend must be one of {tuple(PRODUCT_MODULES)}")
+        self.product_backend = product_backend
         atomic_numbers = tuple(sorted({int(z) for z in atomic_numbers}))
         if not atomic_numbers or atomic_numbers[0] < 0:
             raise ValueError("atomic_numbers must be non-negative and not empty")
@@ -306,7 +323,8 @@ class MACEICTC(nn.Module):
                 num_basis=num_basis, avg_num_neighbors=avg_num_neighbors, use_self_connection=layer > 0 or first_sc,
                 sc_lmax=0 if first_sc else target))
             self.products.append(ProductBlock(channels=channels, lmax=lmax, target_lmax=target,
-                                              correlation=correlation, num_elements=num_elements))
+                                              correlation=correlation, num_elements=num_elements,
+                                              product_backend=product_backend))
         self.layer_readouts = nn.ModuleList([nn.Linear(channels, 1, bias=False)
                                              for _ in range(num_interactions - 1)])
         self.last_readout = nn.Sequential(nn.Linear(channels, readout_hidden, bias=False), NormalizedSiLU(),

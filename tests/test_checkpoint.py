@@ -5,11 +5,12 @@ import pytest
 import torch
 
 
-def _model(seed):
+def _model(seed, product_backend="ictd-pure-u"):
     from mace_ictc.models import MACEICTC
     from oracle.model_ops import OracleOps
     torch.manual_seed(seed)
-    return MACEICTC(channels=8, lmax=2, r_max=3.0, avg_num_neighbors=5.0, ops=OracleOps()).double()
+    return MACEICTC(channels=8, lmax=2, r_max=3.0, avg_num_neighbors=5.0, ops=OracleOps(),
+                    product_backend=product_backend).double()
 
 
 def _system():
@@ -36,6 +37,43 @@ def test_reference_names_round_trip():
     pos, species, src, dst, shift = _system()
     assert torch.allclose(source.energy(pos, species, src, dst, shift), target.energy(pos, species, src, dst, shift),
                           rtol=1e-12, atol=1e-12)
+
+
+@pytest.mark.parametrize("source_backend,target_backend", [("ictd-bridge-u", "ictd-bridge-u"),
+                                                            ("ictd-bridge-u", "ictd-pure-u"),
+                                                            ("ictd-pure-u", "ictd-bridge-u")])
+def test_product_backends_round_trip(source_backend, target_backend):
+    """A bridge-U model writes the reference's bridge-U names (couplings, zero flags,
+    basis bridge); checkpoints of either backend load into a model of either."""
+    from mace_ictc.checkpoint import from_reference_state_dict, model_metadata, to_reference_state_dict
+    source, target = _model(1, source_backend), _model(2, target_backend)
+    ref = to_reference_state_dict(source)
+    if source_backend == "ictd-bridge-u":
+        assert "products.0.symmetric_contractions.symmetric_contractions.contractions.1.U_matrix_3" in ref
+        assert "products.0.symmetric_contractions.symmetric_contractions.contractions.0.weights_max_zeroed" in ref
+        assert "products.1.symmetric_contractions.basis_bridge.q_0" in ref
+    assert model_metadata(target)["ictd_fix_product_backend"] == target_backend
+    from_reference_state_dict(target, ref)
+    pos, species, src, dst, shift = _system()
+    # A new bridge-U block holds the ICTC couplings as FP32-rounded buffers (as the
+    # reference's blocks hold theirs); into pure-U blocks they map against the exact
+    # couplings, so that direction agrees to the couplings' rounding, not to FP64.
+    rtol = 1e-9 if (source_backend, target_backend) == ("ictd-bridge-u", "ictd-pure-u") else 1e-13
+    assert torch.allclose(source.energy(pos, species, src, dst, shift), target.energy(pos, species, src, dst, shift),
+                          rtol=rtol, atol=0)
+
+
+def test_bridge_model_rejects_unknown_product_keys():
+    from mace_ictc.checkpoint import from_reference_state_dict, to_reference_state_dict
+    model = _model(5, "ictd-bridge-u")
+    ref = to_reference_state_dict(model)
+    ref["products.0.symmetric_contractions.symmetric_contractions.contractions.0.extra"] = torch.zeros(1)
+    with pytest.raises(NotImplementedError, match="extra"):
+        from_reference_state_dict(model, ref)
+    ref = to_reference_state_dict(model)
+    del ref["products.1.symmetric_contractions.symmetric_contractions.contractions.0.weights_max"]
+    with pytest.raises(KeyError, match="weights_max"):
+        from_reference_state_dict(model, ref)
 
 
 def test_e3nn_linear_convention():

@@ -18,7 +18,7 @@ from conftest import golden
 CASES = ["model_c8_l2.npz", "model_c8_l3.npz", "model_c8_l2_bridge.npz"]
 
 
-def load_case(name, ops=None, dtype=torch.float64, device="cpu"):
+def load_case(name, ops=None, dtype=torch.float64, device="cpu", product_backend="ictd-pure-u"):
     """(model with the reference weights, species, edges, fixture)."""
     from mace_ictc.checkpoint import from_reference_state_dict
     from mace_ictc.models import MACEICTC
@@ -26,7 +26,8 @@ def load_case(name, ops=None, dtype=torch.float64, device="cpu"):
     state = {k.split(":", 1)[1]: torch.from_numpy(v) for k, v in rec.items()
              if k.startswith("param:") or k.startswith("buffer:")}
     model = MACEICTC(channels=int(rec["channels"]), lmax=int(rec["lmax"]), num_interactions=2, correlation=3,
-                     r_max=float(rec["cutoff"]), avg_num_neighbors=float(rec["avg_num_neighbors"]), ops=ops)
+                     r_max=float(rec["cutoff"]), avg_num_neighbors=float(rec["avg_num_neighbors"]), ops=ops,
+                     product_backend=product_backend)
     model = model.to(dtype)
     from_reference_state_dict(model, {k: v.to(dtype) for k, v in state.items()})
     model = model.to(device)
@@ -34,10 +35,14 @@ def load_case(name, ops=None, dtype=torch.float64, device="cpu"):
     return model, species, rec
 
 
+@pytest.mark.parametrize("product_backend", ["ictd-pure-u", "ictd-bridge-u"])
 @pytest.mark.parametrize("name", CASES)
-def test_model_matches_reference_model(name):
+def test_model_matches_reference_model(name, product_backend):
+    """Every fixture into a model of either product backend (by name, or through the
+    change of coupling basis when bridge-U weights meet pure-U blocks)."""
     from oracle.model_ops import OracleOps
-    model, species, rec = load_case(name, ops=OracleOps())
+    model, species, rec = load_case(name, ops=OracleOps(), product_backend=product_backend)
+    assert model.product_backend == product_backend
     assert not model.interactions[0].self_connection is None            # first-layer self-connection
     pos = torch.from_numpy(rec["pos"]).requires_grad_(True)
     src, dst = torch.from_numpy(rec["src"]), torch.from_numpy(rec["dst"])

@@ -9,9 +9,10 @@ from test_model_reference import CASES, load_case
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("name", CASES)
-def test_cuda_model_matches_reference_model(name, cuda_device):
-    model, species, rec = load_case(name, dtype=torch.float32, device=cuda_device)
+@pytest.mark.parametrize("name,product_backend", [(name, "ictd-pure-u") for name in CASES]
+                         + [("model_c8_l2_bridge.npz", "ictd-bridge-u")])
+def test_cuda_model_matches_reference_model(name, product_backend, cuda_device):
+    model, species, rec = load_case(name, dtype=torch.float32, device=cuda_device, product_backend=product_backend)
     pos = torch.from_numpy(rec["pos"]).float().to(cuda_device).requires_grad_(True)
     src, dst = (torch.from_numpy(rec[k]).to(cuda_device) for k in ("src", "dst"))
     shift = torch.from_numpy(rec["shift"]).float().to(cuda_device)
