@@ -26,7 +26,10 @@ def _positive_int(value, name):
 def create_model(*, channels=64, lmax=3, edge_lmax=None, num_interactions=2, correlation=3, use_reduced_cg=False,
                  atomic_numbers=(1, 6, 8), cutoff=5.0, avg_num_neighbors=50.0, device="cuda",
                  dtype=torch.float32, electrostatics=None):
-    """A freshly initialised MACE-ICTC model on the CUDA backend (not a trained potential)."""
+    """A freshly initialised MACE-ICTC model on the CUDA backend (not a trained potential).
+
+    Bridge-U product blocks, as the reference's factory builds (its couplings are the
+    ICTC ones until a reference checkpoint is loaded)."""
     from .models import MACEICTC
     _positive_int(num_interactions, "num_interactions")
     _positive_int(channels, "channels")
@@ -47,7 +50,8 @@ def create_model(*, channels=64, lmax=3, edge_lmax=None, num_interactions=2, cor
     if dtype != torch.float32 or torch.device(device).type != "cuda":
         raise ValueError("the CUDA backend runs FP32 models on CUDA devices")
     model = MACEICTC(channels=channels, lmax=lmax, num_interactions=num_interactions, correlation=correlation,
-                     r_max=cutoff, avg_num_neighbors=avg_num_neighbors, atomic_numbers=atomic_numbers)
+                     r_max=cutoff, avg_num_neighbors=avg_num_neighbors, atomic_numbers=atomic_numbers,
+                     product_backend="ictd-bridge-u")
     return model.to(device)
 
 

@@ -94,6 +94,7 @@ def test_runtime_energy_and_forces(cuda_device):
     from mace_ictc.systems import random_system
     torch.manual_seed(1)
     model = create_model(channels=32, lmax=2, cutoff=5.0, avg_num_neighbors=40.0, device=cuda_device)
+    assert model.product_backend == "ictd-bridge-u"                   # as the reference's factory
     assert check_model(model)["supported"]
     info = configure_model(model)
     assert info["selected"] == "generated" and all(m._cuda_hp for m in model.modules())
