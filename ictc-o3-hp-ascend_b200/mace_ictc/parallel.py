@@ -11,21 +11,25 @@ returned to their owners (``_reverse`` :455-483).  Energies are summed over owne
 atoms (:632, :646) and the virial is -sum_e r_e (x) dE/dr_e (:660-667).
 
 Every rank holds only its own atoms (``SlabDomain``: global ids, positions and
-species of the owned atoms).  A step is
+species of the owned atoms).  A step (``md_step``) is
 
-1. ``migrate``: atoms that moved into a neighbouring slab are handed to it
-   (ownership changes, reference "changing ownership");
-2. ``halo_layout``: owned atoms within ``halo`` of a face are sent, as position
-   and species rows, to the neighbour on that side, which keeps them as ghosts;
+1. ``exchange_atoms``: atoms that moved into a neighbouring slab are handed to it
+   (ownership changes, reference "changing ownership") and owned atoms within
+   ``halo`` of a face are sent, as position and species rows, to the neighbour on
+   that side, which keeps them as ghosts -- one message per neighbour, after one
+   all_gather of per-rank counts (``migrate`` then ``halo_layout`` is the two-round
+   form it falls back to when an atom moved too far for the single round);
+2. the owned-receiver neighbour list (``slab_edges``);
 3. the model on [owned | left ghosts | right ghosts] with the feature exchange
-   before every later layer (``HaloExchange``) and its adjoint;
+   before every later layer (``HaloExchange``, overlapped with the radial network)
+   and its adjoint;
 4. ``reverse_ghost_forces`` and one all-reduce of energy and virial.
 
 Nothing in a step is proportional to the global atom count.  Transport is
 ``torch.distributed`` point-to-point (``batch_isend_irecv``): NCCL over NVLink
 between GPUs, gloo for CPU tests.  Each exchange packs the rows to send into
-one contiguous buffer per neighbour, so every message is one transfer; sizes
-travel first as one small count message per neighbour, read on the host once.
+one contiguous buffer per neighbour, so every message is one transfer; message
+sizes are known on both sides from counts read on the host once per step.
 """
 from __future__ import annotations
 
