@@ -15,6 +15,7 @@ read once per tile.
 from __future__ import annotations
 
 import itertools
+import weakref
 from functools import lru_cache
 
 import numpy as np
@@ -116,13 +117,13 @@ def block_table(block, device, dtype=torch.float32) -> torch.Tensor:
     cache = block.__dict__.setdefault("_cuda_symmetric_tables", {})
     key = (str(device), dtype)
     hit = cache.get(key)
-    if hit is not None and hit[0] == version:
+    if hit is not None and hit[0] == version and all(r() is u for r, u in zip(hit[2], buffers)):
         return hit[1]
     u64 = {nu: u.detach().double().cpu().numpy() for nu, u in zip(range(1, corr + 1), buffers)}
     output_l = 0 if u64[1].ndim == 2 else (u64[1].shape[0] - 1) // 2
     sym = symmetric_table(u64, output_l, u64[1].shape[-2], corr)
     table = torch.from_numpy(sym.reshape(-1, sym.shape[-1])).to(device=device, dtype=dtype)
-    cache[key] = (version, table)
+    cache[key] = (version, table, tuple(weakref.ref(u) for u in buffers))
     return table
 
 
@@ -433,11 +434,12 @@ def coefficient_table(owner, device):
         return _Fold.apply(usyms, rows, *weights)
     key = (str(device), tuple((p.data_ptr(), p._version) for p in params))
     cached = owner.__dict__.get("_cuda_folded_table")
-    if cached is not None and cached[0] == key and all(a is b for a, b in zip(cached[2], usyms)):
+    if (cached is not None and cached[0] == key and all(a is b for a, b in zip(cached[2], usyms))
+            and len(cached[3]) == len(params) and all(r() is p for r, p in zip(cached[3], params))):
         return cached[1]
     with torch.no_grad():
         table = _Fold.apply(usyms, rows, *[w.detach() for w in weights])
-    owner.__dict__["_cuda_folded_table"] = (key, table, usyms)
+    owner.__dict__["_cuda_folded_table"] = (key, table, usyms, tuple(weakref.ref(p) for p in params))
     return table
 
 

@@ -11,6 +11,7 @@ autograd can differentiate it again.
 from __future__ import annotations
 
 import ctypes
+import weakref
 
 import numpy as np
 import torch
@@ -66,19 +67,24 @@ def pack_image(weights) -> torch.Tensor:
 
 
 class RadialPlan:
-    """Packed image for one set of weights, rebuilt when any weight changes."""
+    """Packed image for one set of weights, rebuilt when any weight changes (another
+    tensor object, an in-place update, another device)."""
 
     def __init__(self):
         self.key = None
+        self.refs = ()
         self.image = None
         self.status = None
 
     def get(self, weights):
         key = tuple((w.data_ptr(), w._version, str(w.device)) for w in weights)
-        if key != self.key:
+        same = key == self.key and len(self.refs) == len(weights) and all(
+            r() is w for r, w in zip(self.refs, weights))
+        if not same:
             self.image = pack_image(weights)
             self.status = torch.zeros(1, dtype=torch.int32, device=weights[0].device)
             self.key = key
+            self.refs = tuple(weakref.ref(w) for w in weights)
         return self.image, self.status
 
 

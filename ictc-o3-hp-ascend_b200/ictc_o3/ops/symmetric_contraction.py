@@ -19,6 +19,7 @@ and shapes).
 """
 from __future__ import annotations
 
+import weakref
 from typing import Dict
 
 import numpy as np
@@ -169,13 +170,13 @@ class _BridgeUContraction(_ICTDPureUContraction):
         version = tuple((u.data_ptr(), u._version, tuple(u.shape)) for u in buffers)
         key = (str(device), dtype)
         cached = self._table_cache.get(key)
-        if cached is not None and cached[0] == version:
+        if cached is not None and cached[0] == version and all(r() is u for r, u in zip(cached[2], buffers)):
             return cached[1]
         from ictc_o3.backends.cuda.contraction import symmetric_table
         u64 = {nu: u.detach().double().cpu().numpy() for nu, u in zip(range(1, self.correlation + 1), buffers)}
         sym = symmetric_table(u64, self.output_l, u64[1].shape[-2], self.correlation)
         table = torch.from_numpy(sym.reshape(-1, sym.shape[-1])).to(device=device, dtype=dtype)
-        self._table_cache[key] = (version, table)
+        self._table_cache[key] = (version, table, tuple(weakref.ref(u) for u in buffers))
         return table
 
 
