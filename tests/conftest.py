@@ -14,6 +14,14 @@ GOLDEN = os.path.join(REPO, "tests", "golden")
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200) and libictc_cuda.so")
+    config.addinivalue_line("markers", "multigpu: starts one NCCL rank process per GPU on several GPUs")
+
+
+def pytest_collection_modifyitems(config, items):
+    """Tests that start rank processes on several GPUs run after all the others (they
+    are the slowest and need the most of the box), keeping the collection order
+    otherwise."""
+    items.sort(key=lambda item: item.get_closest_marker("multigpu") is not None)
 
 
 def golden(name):

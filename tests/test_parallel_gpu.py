@@ -115,6 +115,7 @@ def _run_ranks(worker, args, world, deadline_s=300.0):
         raise
 
 
+@pytest.mark.multigpu
 @pytest.mark.parametrize("world,x_fraction", [(2, 1.0), (4, 1.0), (8, 1.0), (4, 0.45)])
 def test_nccl_ranks_match_one_gpu(world, x_fraction, cuda_device, tmp_path):
     """world ranks on world GPUs equal one GPU: energy 1e-5, forces and virial 1e-4, and
