@@ -3,7 +3,8 @@
 ``ictc_neighbor_list_noalloc`` serves callers that cannot allocate device memory
 while they run (an MD engine that owns all device buffers, or a host program
 using the C library without an allocator for scratch): its scratch is a fixed
-array inside the library.  This file is collected last on purpose.
+array inside the library.  This file is collected last on purpose; only the
+multi-GPU rank tests, which run in processes of their own, follow it.
 """
 import ctypes
 
