@@ -7,6 +7,7 @@ every operator runs through libictc_cuda.so.  There is no host fallback.
 import torch
 import torch.nn.functional as F
 
+from ictc_o3.backends.cuda.linear import channel_linear, species_channel_linear
 from ictc_o3.backends.cuda.runtime import require_cuda_fp32, strict_fp32
 
 
@@ -221,4 +222,5 @@ def normalized_silu(features, scale=1.):
 
 
 __all__ = ["EdgeTensorProduct", "PackedGraphMessage", "GraphMessage", "direction_harmonics",
-           "create_symmetric_contraction", "configure_symmetric_contraction", "normalized_silu", "strict_fp32"]
+           "create_symmetric_contraction", "configure_symmetric_contraction",
+           "channel_linear", "species_channel_linear", "normalized_silu", "strict_fp32"]

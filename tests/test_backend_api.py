@@ -39,6 +39,29 @@ SIGNATURES = [
 ]
 
 
+# ictc_o3/operators.py:232-234 and mace_ictc/hp/__init__.py of the reference (the mesh
+# electrostatics the reference's ictc_o3 package adds are not part of this backend)
+PUBLIC_OPERATORS = ["EdgeTensorProduct", "PackedGraphMessage", "GraphMessage", "direction_harmonics",
+                    "create_symmetric_contraction", "configure_symmetric_contraction",
+                    "channel_linear", "species_channel_linear", "normalized_silu", "strict_fp32"]
+
+
+def test_public_import_paths():
+    """The reference's import paths: ``from ictc_o3 import ...``, ``ictc_o3.operators``,
+    ``mace_ictc.hp`` and ``mace_ictc.hp.runtime``."""
+    import ictc_o3
+    import ictc_o3.operators as operators
+    import mace_ictc.hp as hp
+    import mace_ictc.hp.runtime as hp_runtime
+    import mace_ictc.runtime as runtime
+    assert operators.__all__ == PUBLIC_OPERATORS and ictc_o3.__all__ == PUBLIC_OPERATORS
+    for name in PUBLIC_OPERATORS:
+        assert getattr(ictc_o3, name) is getattr(operators, name)
+    assert hp.__all__ == [*PUBLIC_OPERATORS, "check_model", "configure_model", "create_model", "energy_and_forces"]
+    for name in ("create_model", "energy_and_forces", "check_model", "configure_model"):
+        assert getattr(hp, name) is getattr(runtime, name) is getattr(hp_runtime, name)
+
+
 @pytest.mark.parametrize("module,name,positional,keyword", SIGNATURES, ids=[s[1] for s in SIGNATURES])
 def test_reference_signature(module, name, positional, keyword):
     import importlib
