@@ -223,3 +223,35 @@ def test_reference_layout_owner_gives_the_same_contraction(name):
     with torch.no_grad():
         out = polynomial(torch.from_numpy(rec["x"]), table, tiles, tile_species, contraction_spec(owner)[:4])
     torch.testing.assert_close(out, torch.from_numpy(rec["out"]), rtol=1e-10, atol=1e-11)
+
+
+def test_folded_table_cache(monkeypatch):
+    """``coefficient_table``'s cache (host logic; the fold itself replaced by its torch
+    definition, T_t = Usym_t W_t, since the kernel needs a GPU): kept for frozen
+    weights, rebuilt when a weight changes in place or is replaced, or when a block's
+    coupling table is rebuilt; never cached while a weight needs a gradient."""
+    from ictc_o3.backends.cuda import contraction as cc
+
+    class TorchFold(torch.autograd.Function):
+        @staticmethod
+        def forward(ctx, usyms, rows, *weights):
+            return torch.cat([torch.matmul(u.unsqueeze(0).to(w.dtype), w) for u, w in zip(usyms, weights)], 1)
+
+    monkeypatch.setattr(cc, "_Fold", TorchFold)
+    rec = golden(CASES[0])
+    module = _module(rec)
+    with torch.no_grad():
+        first = cc.coefficient_table(module, torch.device("cpu"))
+        assert cc.coefficient_table(module, torch.device("cpu")) is first
+        module.contractions[0].weights_max.mul_(2.0)                       # in-place update
+        second = cc.coefficient_table(module, torch.device("cpu"))
+        assert second is not first and not torch.equal(second, first)
+        old = module.contractions[1].weights[0]
+        module.contractions[1].weights[0] = torch.nn.Parameter(old.detach().clone())   # new tensor object
+        assert cc.coefficient_table(module, torch.device("cpu")) is not second
+        third = cc.coefficient_table(module, torch.device("cpu"))
+        module.contractions[2].U_matrix_2.mul_(0.5)                          # couplings change
+        fourth = cc.coefficient_table(module, torch.device("cpu"))
+        assert fourth is not third and not torch.equal(fourth, third)
+    live = cc.coefficient_table(module, torch.device("cpu"))                # weights require grad
+    assert live.requires_grad and module.__dict__["_cuda_folded_table"][1] is fourth
