@@ -123,3 +123,25 @@ def test_radial_rejects_unsupported_shapes():
     assert lib.ictc_radial_image_bytes(8, 64, 100) == -1
     assert lib.ictc_radial_image_bytes(8, 64, 96) == -1
     assert lib.ictc_radial_forward(None, None, None, 10, 8, 64, 192, None, None) == -1
+
+
+def test_radial_plan_repacks_only_when_weights_change():
+    """RadialPlan keeps one packed image per set of weight tensors: the same tensors
+    reuse it; an in-place update, a replaced tensor or padded widths repack (host only)."""
+    import torch
+    from ictc_o3.backends.cuda import radial
+    torch.manual_seed(1)
+    layers = [torch.nn.Linear(8, 64, bias=False), torch.nn.Linear(64, 64, bias=False),
+              torch.nn.Linear(64, 64, bias=False), torch.nn.Linear(64, 88, bias=False)]
+    weights = [m.weight for m in layers]
+    plan = radial.RadialPlan()
+    image, status = plan.get(weights)
+    assert plan.get([m.weight for m in layers])[0] is image              # same tensors: reused
+    with torch.no_grad():
+        layers[2].weight.mul_(0.5)                                        # in-place update
+    second, _ = plan.get(weights)
+    assert second is not image and not torch.equal(second, image)
+    layers[1].weight = torch.nn.Parameter(layers[1].weight.detach().clone())   # replaced tensor
+    third, _ = plan.get([m.weight for m in layers])
+    assert third is not second and torch.equal(third, second)
+    assert radial.padded_gates(88) == 128 and third.numel() == _native_size(8, 64, 128)
