@@ -1,5 +1,5 @@
-"""The torch restatement of the edge geometry used by the differentiable (second-order)
-path equals the model's radial embedding, which the reference-model fixtures pin, in
+"""Torch restatements used by the differentiable (second-order) paths: the edge geometry
+and the radial network equal the model formulas the reference-model fixtures pin, in
 value and in first and second derivatives (CPU, FP64)."""
 import pytest
 import torch
@@ -30,3 +30,25 @@ def test_edge_geometry_reference_matches_model_embedding(basis_norm):
     (h1,) = torch.autograd.grad((g1 * V).sum(), [vec], retain_graph=True)
     (h2,) = torch.autograd.grad((g2 * V).sum(), [vec])
     torch.testing.assert_close(h1, h2, rtol=1e-9, atol=1e-10)
+
+
+def test_radial_reference_matches_model_network():
+    """The radial network's torch restatement (second-order path) is the model's ``fc``
+    (Linear, normalised SiLU x 3, Linear; ``pure_cartesian_ictd_fix.py:1545-1553``)."""
+    from ictc_o3.backends.cuda.radial import mlp_reference
+    from mace_ictc.models import InteractionBlock
+    torch.manual_seed(2)
+    block = InteractionBlock(channels=8, lmax=2, input_lmax=2, num_elements=3, num_basis=8,
+                             avg_num_neighbors=5.0, use_self_connection=True, sc_lmax=2).double()
+    linears = [m for m in block.fc if isinstance(m, torch.nn.Linear)]
+    feats = torch.randn(50, 8, dtype=torch.float64, requires_grad=True)
+    want = block.fc(feats)
+    got = mlp_reference(feats, [m.weight for m in linears])
+    torch.testing.assert_close(got, want, rtol=1e-13, atol=1e-14)
+    G = torch.randn_like(want)
+    (g1,) = torch.autograd.grad(got, [feats], G, create_graph=True)
+    (g2,) = torch.autograd.grad(want, [feats], G, create_graph=True)
+    torch.testing.assert_close(g1, g2, rtol=1e-12, atol=1e-13)
+    (h1,) = torch.autograd.grad(g1.sum(), [feats])
+    (h2,) = torch.autograd.grad(g2.sum(), [feats])
+    torch.testing.assert_close(h1, h2, rtol=1e-11, atol=1e-12)
