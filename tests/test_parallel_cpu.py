@@ -18,8 +18,10 @@ import torch.multiprocessing as mp
 R_MAX = 3.0
 
 
-def _system(n_atoms=100, density=0.1, min_dist=0.9, seed=0, x_fraction=1.0):
-    """Random atoms in a periodic cube; ``x_fraction`` < 1 leaves the rest of x empty."""
+def _system(n_atoms=100, density=0.1, min_dist=0.9, seed=0, x_fraction=1.0, faces=0):
+    """Random atoms in a periodic cube; ``x_fraction`` < 1 leaves the rest of x empty;
+    ``faces`` = world puts atoms exactly on the slab faces (x = k side / world), at
+    x = side and just below it."""
     gen = torch.Generator().manual_seed(seed)
     side = (n_atoms / density) ** (1.0 / 3.0)
     scale = torch.tensor([side * x_fraction, side, side], dtype=torch.float64)
@@ -31,6 +33,10 @@ def _system(n_atoms=100, density=0.1, min_dist=0.9, seed=0, x_fraction=1.0):
         if pos.shape[0] == 0 or float(d.norm(dim=1).min()) >= min_dist:
             pos = torch.cat([pos, cand])
     species = torch.randint(0, 3, (n_atoms,), generator=gen)
+    if faces:
+        xs = [side * k / faces for k in range(faces + 1)] + [side * (1.0 - 1e-15), 0.5 * side / faces]
+        for i, x in enumerate(xs):
+            pos[i, 0] = x
     return pos, species, side
 
 
@@ -177,6 +183,16 @@ def test_empty_ranks(tmp_path):
     outs = _run(world, tmp_path, case)
     assert sum(out["ids"].numel() == 0 for out in outs) >= 1
     _check_against_single(outs, n_atoms, _system(n_atoms, seed=5)[2])
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_atoms_on_slab_faces(world, tmp_path):
+    """Atoms exactly on slab faces and on the periodic boundary: each is owned by one
+    rank after the step's exchange, and the result equals the single process."""
+    n_atoms = 120
+    case = {"system": {"n_atoms": n_atoms, "seed": 7, "faces": world}}
+    outs = _run(world, tmp_path, case)
+    _check_against_single(outs, n_atoms, _system(n_atoms, seed=7)[2])
 
 
 def test_thin_slabs_are_rejected():
