@@ -100,11 +100,23 @@ def _bridge_weights(module, tensors: Dict[str, torch.Tensor], where: str) -> Dic
     return out
 
 
-def _load_bridge_module(module, sub: Dict[str, torch.Tensor], prefix: str, strict: bool, unknown: List[str]):
+def _require_couplings(module, sub: Dict[str, torch.Tensor], prefix: str):
+    lacking = [prefix + n for n in module.state_dict() if ".U_matrix_" in n and n not in sub]
+    if lacking:
+        raise KeyError(f"bridge-U checkpoint lacks its couplings: {lacking}")
+
+
+def _load_bridge_module(module, sub: Dict[str, torch.Tensor], prefix: str, strict: bool, unknown: List[str],
+                        bridge_named: bool):
     """Load reference product-block tensors (bridge-U names, or pure-U names moved
     under ``symmetric_contractions.``) into a bridge-U product module of this model:
     couplings, weights, zero flags and bridge matrices by name, coupling counts
-    resized to the checkpoint's."""
+    resized to the checkpoint's.  Bridge-U weights mean nothing without their own
+    couplings, so a bridge-U block must bring every ``U_matrix_nu`` (checked before
+    anything is loaded); a pure-U block without them keeps the ICTC couplings, which
+    are its own."""
+    if bridge_named:
+        _require_couplings(module, sub, prefix)
     result = module.load_state_dict(sub, strict=False)
     unknown.extend(prefix + k for k in result.unexpected_keys)
     if strict:
@@ -131,6 +143,7 @@ def from_reference_state_dict(model, state: Dict[str, torch.Tensor], strict: boo
     element_blocks: Dict[str, Dict[int, torch.Tensor]] = {}
     bridge: Dict[tuple, Dict[str, torch.Tensor]] = {}
     direct: Dict[int, Dict[str, torch.Tensor]] = {}     # product blocks of a bridge-U model, by name
+    bridge_named: set = set()                           # ... of those, the ones given under bridge-U names
     loaded: set = set()
 
     def bridge_model(i: int) -> bool:
@@ -144,6 +157,8 @@ def from_reference_state_dict(model, state: Dict[str, torch.Tensor], strict: boo
                          r"(symmetric_contractions\.contractions\.(\d+)\.(.+)|basis_bridge\.q_\d+)", key)
         if m and bridge_model(int(m[1])):
             direct.setdefault(int(m[1]), {})[m[2]] = value
+            if m[3] is not None:
+                bridge_named.add(int(m[1]))
             continue
         if m and m[3] is None:
             accepted.append(key)                         # already folded into the U buffers
@@ -201,9 +216,12 @@ def from_reference_state_dict(model, state: Dict[str, torch.Tensor], strict: boo
         where = f"products.{i}.symmetric_contractions.symmetric_contractions.contractions.{t}"
         for name, value in _bridge_weights(module, tensors, where).items():
             target[f"products.{i}.symmetric_contractions.contractions.{t}.{name}"] = value
+    for i in bridge_named:                              # before any block is loaded
+        _require_couplings(model.products[i].symmetric_contractions, direct[i], f"products.{i}.symmetric_contractions.")
     for i, sub in direct.items():
         prefix = f"products.{i}.symmetric_contractions."
-        _load_bridge_module(model.products[i].symmetric_contractions, sub, prefix, strict, unknown)
+        _load_bridge_module(model.products[i].symmetric_contractions, sub, prefix, strict, unknown,
+                            i in bridge_named)
         loaded.update(prefix + n for n, _ in model.products[i].symmetric_contractions.named_parameters())
     if strict and unknown:
         raise NotImplementedError(f"reference keys without a counterpart in this model: {unknown}")

@@ -74,6 +74,12 @@ def test_bridge_model_rejects_unknown_product_keys():
     del ref["products.1.symmetric_contractions.symmetric_contractions.contractions.0.weights_max"]
     with pytest.raises(KeyError, match="weights_max"):
         from_reference_state_dict(model, ref)
+    ref = to_reference_state_dict(model)
+    del ref["products.0.symmetric_contractions.symmetric_contractions.contractions.2.U_matrix_3"]
+    before = {k: v.clone() for k, v in model.state_dict().items()}
+    with pytest.raises(KeyError, match="couplings"):                  # bridge weights without their U
+        from_reference_state_dict(model, ref)
+    assert all(torch.equal(before[k], v) for k, v in model.state_dict().items() if k.startswith("products."))
 
 
 def test_e3nn_linear_convention():
