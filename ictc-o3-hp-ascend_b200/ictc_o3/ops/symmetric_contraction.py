@@ -118,7 +118,8 @@ class _BridgeUContraction(_ICTDPureUContraction):
     ``weights[idx]``, ``weights_max_zeroed`` guards ``weights_max``): a flagged
     weight is held at zero and is not trained.  A loaded state dict whose coupling
     count P differs from this block's (the reference's reduced-CG option) resizes the
-    U buffers and weights to it.
+    U buffers and weights to it; the resized weights are new parameter objects, so
+    such a state dict is loaded before an optimizer is built over the module.
     """
 
     def __init__(self, **kwargs):
