@@ -211,7 +211,9 @@ int ictc_sc_backward(const float* x, const float* table, const int64_t* tiles, c
  *                (the weight gradient: table holds dT, weights receives dW)
  * usym [rows, cols] (symmetrised couplings, rows = monomials x (2t+1)),
  * weights [species, cols, channels], table [species, table_rows, channels].
- * Deterministic (no atomics). */
+ * The couplings may be either of the reference's parameterisations (pure-ICTC U,
+ * or bridge-U with its basis bridge folded in, ictc_o3/ops/symmetric_contraction.py:92-206):
+ * the kernels only see their symmetrised rows.  Deterministic (no atomics). */
 int ictc_sc_fold(const float* usym, const float* weights, float* table, int rows, int cols, int channels,
                  int species, int64_t table_rows, int64_t row0, int adjoint, void* stream);
 
