@@ -23,6 +23,7 @@ import torch
 
 from ictc_o3.autograd.adjoint_requirements import required_gradients
 from . import _native
+from .cache import cache_of
 from ._native import ptr, stream_of
 
 
@@ -114,7 +115,7 @@ def block_table(block, device, dtype=torch.float32) -> torch.Tensor:
     corr = int(block.correlation)
     buffers = [block.U_tensors(nu) for nu in range(1, corr + 1)]
     version = tuple((u.data_ptr(), u._version, tuple(u.shape)) for u in buffers)
-    cache = block.__dict__.setdefault("_cuda_symmetric_tables", {})
+    cache = cache_of(block, "_cuda_symmetric_tables")
     key = (str(device), dtype)
     hit = cache.get(key)
     if hit is not None and hit[0] == version and all(r() is u for r, u in zip(hit[2], buffers)):
@@ -433,13 +434,14 @@ def coefficient_table(owner, device):
     if live:
         return _Fold.apply(usyms, rows, *weights)
     key = (str(device), tuple((p.data_ptr(), p._version) for p in params))
-    cached = owner.__dict__.get("_cuda_folded_table")
+    store = cache_of(owner, "_cuda_folded_table")
+    cached = store.get("table")
     if (cached is not None and cached[0] == key and all(a is b for a, b in zip(cached[2], usyms))
             and len(cached[3]) == len(params) and all(r() is p for r, p in zip(cached[3], params))):
         return cached[1]
     with torch.no_grad():
         table = _Fold.apply(usyms, rows, *[w.detach() for w in weights])
-    owner.__dict__["_cuda_folded_table"] = (key, table, usyms, tuple(weakref.ref(p) for p in params))
+    store["table"] = (key, table, usyms, tuple(weakref.ref(p) for p in params))
     return table
 
 

@@ -20,6 +20,7 @@ from typing import Dict, Optional
 import torch
 
 from . import _native
+from .cache import cache_of
 from ._native import ptr, stream_of
 from .tensor_product import (_weight_and_gates, _check, get_plan, product, split_output)
 
@@ -219,8 +220,9 @@ def radial_graph_message(owner, features: Dict[int, torch.Tensor], harmonics: Di
     shape = (linears[0].in_features, linears[0].out_features, linears[-1].out_features)
     if not radial_kernels.supported(*shape):
         return None
-    plan = radial.__dict__.get("_ictc_radial_plan")
+    store = cache_of(radial, "_ictc_radial_plan")
+    plan = store.get("plan")
     if plan is None:
-        plan = radial.__dict__["_ictc_radial_plan"] = radial_kernels.RadialPlan()
+        plan = store["plan"] = radial_kernels.RadialPlan()
     gates = radial_kernels.radial_gates(linears, edge_features, plan)
     return graph_message(owner, features, harmonics, gates, src, dst, mask, edge_chunk_size=edge_chunk_size)

@@ -11,6 +11,8 @@ import weakref
 
 import torch
 
+from .cache import cache_of
+
 
 def validate_species(index: torch.Tensor, count: int):
     """Raise if an element index lies outside [0, count)."""
@@ -30,7 +32,8 @@ def compact_species(owner, atomic_numbers: torch.Tensor) -> torch.Tensor:
     atomic-number tensor, table and element count."""
     table = owner.atomic_number_to_index
     stamp = (atomic_numbers._version, table._version, int(owner.num_elements), atomic_numbers.device)
-    memo = owner.__dict__.get("_cuda_species_memo")
+    store = cache_of(owner, "_cuda_species_memo")
+    memo = store.get("memo")
     if memo is not None and memo[0]() is atomic_numbers and memo[1] == stamp and memo[2]._version == memo[3]:
         return memo[2]
     z = atomic_numbers.to(torch.int64)
@@ -40,5 +43,5 @@ def compact_species(owner, atomic_numbers: torch.Tensor) -> torch.Tensor:
     if index.numel() and bool(((index < 0) | (index >= owner.num_elements)).any()):
         raise ValueError("Atomic numbers are outside the model's compact mapping")
     index._ictc_cuda_valid_species = (int(owner.num_elements), index._version)
-    owner.__dict__["_cuda_species_memo"] = (weakref.ref(atomic_numbers), stamp, index, index._version)
+    store["memo"] = (weakref.ref(atomic_numbers), stamp, index, index._version)
     return index

@@ -23,6 +23,7 @@ import torch
 
 from ictc_o3.autograd.adjoint_requirements import required_gradients
 from . import _native
+from .cache import cache_of
 from ._native import ptr, stream_of
 
 LAYOUTS = {"ir_mul": 0, "mul_ir": 1}
@@ -103,7 +104,7 @@ def get_plan(owner, layout: str, device: torch.device, cpl_forward: int = 0, cpl
         raise ValueError("The CUDA tensor product requires CUDA tensors")
     index = device.index if device.index is not None else torch.cuda.current_device()
     key = (index, layout, tuple(tuple(p) for p in owner.paths), int(owner.channels), cpl_forward, cpl_backward)
-    cache = owner.__dict__.setdefault("_cuda_tp_plans", {})
+    cache = cache_of(owner, "_cuda_tp_plans")
     plan = cache.get(key)
     if plan is None:
         plan = TPPlan(owner, layout, torch.device("cuda", index), cpl_forward, cpl_backward)

@@ -27,6 +27,7 @@ import torch
 import torch.nn as nn
 
 from ictc_o3.basis.ictd_irreps import ictd_u_matrix_so3
+from ictc_o3.backends.cuda.cache import cache_of
 
 
 class _ICTDPureUContraction(nn.Module):
@@ -47,7 +48,6 @@ class _ICTDPureUContraction(nn.Module):
         for nu in range(self.correlation - 1, 0, -1):
             num = self.U_tensors(nu).shape[-1]
             self.weights.append(nn.Parameter(torch.randn(num_elements, num, num_features) / max(num, 1)))
-        self._table_cache = {}
 
     def U_tensors(self, nu: int) -> torch.Tensor:
         return getattr(self, f"U_matrix_{nu}")
@@ -59,13 +59,14 @@ class _ICTDPureUContraction(nn.Module):
     def symmetric_table(self, device, dtype=torch.float32) -> torch.Tensor:
         """Symmetrised U in the kernel's row order, [rows * (2t+1), sum P] (cached per device, dtype)."""
         key = (str(device), dtype)
-        table = self._table_cache.get(key)
+        cache = cache_of(self, "_table_cache")
+        table = cache.get(key)
         if table is None:
             from ictc_o3.backends.cuda.contraction import symmetric_table
             dim = self._u64[1].shape[-2]
             sym = symmetric_table(self._u64, self.output_l, dim, self.correlation)
             table = torch.from_numpy(sym.reshape(-1, sym.shape[-1])).to(device=device, dtype=dtype)
-            self._table_cache[key] = table
+            cache[key] = table
         return table
 
 
@@ -170,14 +171,15 @@ class _BridgeUContraction(_ICTDPureUContraction):
         buffers = [self.U_tensors(nu) for nu in range(1, self.correlation + 1)]
         version = tuple((u.data_ptr(), u._version, tuple(u.shape)) for u in buffers)
         key = (str(device), dtype)
-        cached = self._table_cache.get(key)
+        cache = cache_of(self, "_table_cache")
+        cached = cache.get(key)
         if cached is not None and cached[0] == version and all(r() is u for r, u in zip(cached[2], buffers)):
             return cached[1]
         from ictc_o3.backends.cuda.contraction import symmetric_table
         u64 = {nu: u.detach().double().cpu().numpy() for nu, u in zip(range(1, self.correlation + 1), buffers)}
         sym = symmetric_table(u64, self.output_l, u64[1].shape[-2], self.correlation)
         table = torch.from_numpy(sym.reshape(-1, sym.shape[-1])).to(device=device, dtype=dtype)
-        self._table_cache[key] = (version, table, tuple(weakref.ref(u) for u in buffers))
+        cache[key] = (version, table, tuple(weakref.ref(u) for u in buffers))
         return table
 
 

@@ -32,6 +32,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from ictc_o3.backends.cuda.cache import cache_of
 from ictc_o3.basis.ictd_irreps import EdgeWeightedPathPreservingTensorProduct, operator_paths
 from ictc_o3.ops.symmetric_contraction import (ICTDBridgeUSymmetricContractionSO3,
                                                ICTDPureUSymmetricContractionSO3)
@@ -64,12 +65,13 @@ class CudaOps:
         from ictc_o3.backends.cuda import radial
         linears = [m for m in fc if isinstance(m, nn.Linear)]
         shape = (linears[0].in_features, linears[0].out_features, linears[-1].out_features)
-        plan = fc.__dict__.get("_ictc_radial_plan")
+        store = cache_of(fc, "_ictc_radial_plan")
+        plan = store.get("plan")
         if plan is None:
             if not radial.supported(*shape):
                 raise ValueError(f"radial MLP shape (features, hidden, gates) = {shape} is not supported by the "
                                  "fused radial kernels")
-            plan = fc.__dict__["_ictc_radial_plan"] = radial.RadialPlan()
+            plan = store["plan"] = radial.RadialPlan()
         return radial.radial_gates(linears, feats, plan)
 
 

@@ -254,4 +254,4 @@ def test_folded_table_cache(monkeypatch):
         fourth = cc.coefficient_table(module, torch.device("cpu"))
         assert fourth is not third and not torch.equal(fourth, third)
     live = cc.coefficient_table(module, torch.device("cpu"))                # weights require grad
-    assert live.requires_grad and module.__dict__["_cuda_folded_table"][1] is fourth
+    assert live.requires_grad and cc.cache_of(module, "_cuda_folded_table")["table"][1] is fourth

@@ -128,3 +128,26 @@ def test_force_loss_training_gradients_match_oracle(lmax, cuda_device):
             continue
         assert a is not None, name
         assert_close(a.cpu(), b, 1e-4, None, f"d loss / d {name}")
+
+
+def test_model_copies_after_running(cuda_device):
+    """A model that has run (device plans, packed radial weights, folded tables cached on
+    it) deep-copies and saves whole; the copies rebuild their own state and give the
+    same energies and forces."""
+    import copy
+    import io
+    pos, species, side = random_system(30, seed=11)
+    src, dst, shift = brute_neighbors(pos, side, 5.0)
+    args = [t.to(cuda_device) for t in (pos.float(), species, src, dst, shift.float())]
+    model, _ = build_models(lmax=2)
+    model = model.to(cuda_device)
+    e, f = model.energy_and_forces(*args)
+    twin = copy.deepcopy(model)
+    buf = io.BytesIO()
+    torch.save(model, buf)
+    buf.seek(0)
+    loaded = torch.load(buf, weights_only=False)
+    for other in (twin, loaded):
+        e2, f2 = other.energy_and_forces(*args)
+        assert_close(e2.detach().cpu(), e.detach().cpu(), 1e-6, None, "energy of the copy")
+        assert_close(f2.detach().cpu(), f.detach().cpu(), 1e-6, None, "forces of the copy")
