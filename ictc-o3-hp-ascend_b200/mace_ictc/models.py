@@ -26,7 +26,6 @@ with the oracle ops) the same modules use plain torch matrix products.
 from __future__ import annotations
 
 import math
-from typing import Optional
 
 import torch
 import torch.nn as nn
